@@ -1,0 +1,161 @@
+/*
+ * tjb200.h -- C ABI of libtjb200.so, the sm_100a (B200) kernels behind the
+ * fused causal Transformer-encoder forward.
+ *
+ * The reference project (tjkernels, TechJam 2026) has no compiled code: its
+ * kernel layer is a Python facade over Triton kernels.  Each entry point
+ * below replaces one function of that facade; the facade signature it stands
+ * in for is cited beside it (paths inside the reference project).
+ *
+ * Conventions (all entry points):
+ *   - Plain device pointers and sizes; no framework types.  The caller owns
+ *     and allocates every buffer (outputs included).  The library never
+ *     allocates device memory, never synchronises the stream and launches
+ *     only on the stream it is given, so every call may be captured in a CUDA
+ *     graph.
+ *   - Return 0 (TJB_OK) on success, otherwise a tjb_status code; no exception
+ *     crosses the ABI.  tjb_status_string() names a code.
+ *   - Dtype codes: TJB_F32 = 0, TJB_F16 = 1, TJB_BF16 = 2.
+ *   - Row-major matrices; leading dimensions are in elements.  Tensor-memory
+ *     (TMA) operands need 16-byte aligned base pointers and row pitches.
+ *   - Device-side waits are bounded.  A wait that runs out records
+ *     TJB_ERR_DEVICE_TIMEOUT in a device status word that
+ *     tjb_device_status() reads back (that call synchronises the device).
+ *   - Functions are thread-compatible: concurrent calls on different streams
+ *     are safe; internal caches are mutex-guarded.
+ */
+#ifndef TJB200_H
+#define TJB200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* tjb_stream_t; /* == cudaStream_t */
+
+enum tjb_status {
+  TJB_OK = 0,
+  TJB_ERR_INVALID_ARGUMENT = 1,  /* null pointer or negative size */
+  TJB_ERR_BAD_SHAPE = 2,         /* shape outside the kernel's contract */
+  TJB_ERR_BAD_ALIGNMENT = 3,     /* pointer or pitch not 16-byte aligned */
+  TJB_ERR_UNSUPPORTED_DTYPE = 4,
+  TJB_ERR_LAUNCH = 5,            /* CUDA reported a launch error */
+  TJB_ERR_TENSOR_MAP = 6,        /* cuTensorMapEncodeTiled failed */
+  TJB_ERR_DEVICE_TIMEOUT = 7,    /* a bounded device-side wait ran out */
+  TJB_ERR_NO_DEVICE = 8,         /* no sm_100 device current */
+  TJB_ERR_NON_PREFIX_MASK = 9    /* reported by tjb_mask_lengths' flag word */
+};
+
+enum tjb_dtype { TJB_F32 = 0, TJB_F16 = 1, TJB_BF16 = 2 };
+
+/* Library version (major*10000 + minor*100 + patch). */
+int tjb_version(void);
+
+/* Human-readable name of a tjb_status code (static storage). */
+const char* tjb_status_string(int status);
+
+/*
+ * Fused residual-add + LayerNorm over rows of length d.
+ *   x        = res + delta            (delta may be NULL: x = res)
+ *   res_out  = x                      (skipped when res_out is NULL)
+ *   out      = (x - mean(x)) * rsqrt(var(x) + eps) * w + b   in out_dtype
+ * Statistics in fp32.  When row_mask is non-NULL, rows with row_mask[r] == 0
+ * get out = 0 exactly (the final padded-row zeroing of the forward).
+ * res / res_out: fp32 [rows, d]; delta: delta_dtype [rows, d]; w, b: fp32 [d];
+ * out: out_dtype [rows, d].  Needs d % 4 == 0 and d <= 8192; res_out may
+ * alias res.
+ * Replaces fused_add_layernorm(residual, delta, weight, bias, eps, out_dtype,
+ * write_residual) -- tjkernels/kernels/__init__.py:48-70 and
+ * tjkernels/kernels/layernorm.py:86-127; the row zeroing replaces
+ * out.masked_fill(~mask[..., None], 0) at tjkernels/engine.py:267-268.
+ */
+int tjb_add_layernorm(const float* res, const void* delta, float* res_out, void* out,
+                      const float* w, const float* b, int64_t rows, int d, float eps,
+                      int delta_dtype, int out_dtype, const uint8_t* row_mask,
+                      tjb_stream_t stream);
+
+/*
+ * C[M, N] = act(A[M, K] * B[N, K]^T + bias[N])   on tcgen05 tensor cores.
+ * A, B: f16 or bf16 (same type), K-major (K contiguous; B is the nn.Linear
+ * weight layout [out, in]).  bias: fp32 [N] or NULL.  act: 0 = none,
+ * 1 = exact erf GELU.  C: out_dtype (f32, or the input type).
+ * Accumulation in fp32.  Needs K % 8 == 0, N % 8 == 0, lda/ldb/ldc multiples
+ * of 8 elements.
+ * Replaces the packed-QKV and out-projection torch.addmm calls
+ * (tjkernels/engine.py:245,247) and the unfused FFN fallback
+ * addmm -> gelu -> addmm (tjkernels/kernels/__init__.py:88-89).
+ */
+int tjb_gemm_bias(const void* A, const void* B, const float* bias, void* C,
+                  int M, int N, int K, int lda, int ldb, int ldc,
+                  int in_dtype, int out_dtype, int act, tjb_stream_t stream);
+
+/*
+ * Causal (or full) multi-head attention forward on tcgen05 tensor cores,
+ * reading Q, K and V in place from the packed QKV projection output.
+ *   qkv: [B, S, 3, H, hd] in dtype (f16 or bf16), row pitch 3*H*hd
+ *   out: [B*S, H*hd] in dtype; out[b*S + i, h*hd + c]
+ *   out = softmax(Q K^T * scale  (+ masking)) V   per (b, h)
+ * Masking: causal (key j visible to query i iff j <= i) when causal != 0;
+ * lengths (int32 [B], nullable) restricts keys to j < lengths[b];
+ * key_mask (uint8 [B, S], nullable) hides keys with key_mask == 0.
+ * mask_flags (int32, nullable, device) is the flag word written by
+ * tjb_mask_lengths: when it reads 0 the mask is a prefix mask and query tiles
+ * wholly at or past lengths[b] are skipped (their rows are written as 0).
+ * Needs hd in {64, 128}.
+ * Replaces flash_attention(qkv, heads, causal) --
+ * tjkernels/kernels/attention.py:189-226 (kernel :34-125) -- and the
+ * masked SDPA fallback at tjkernels/engine.py:184-203.
+ */
+int tjb_flash_fwd(const void* qkv, void* out, int B, int S, int H, int hd,
+                  float scale, int causal, const int32_t* lengths,
+                  const uint8_t* key_mask, const int32_t* mask_flags,
+                  int dtype, tjb_stream_t stream);
+
+/*
+ * Feed-forward block out = gelu_erf(h * w1^T + b1) * w2^T + b2.
+ * h: [T, d]; w1: [F, d]; w2: [d, F] (nn.Linear layouts, f16/bf16);
+ * b1: fp32 [F]; b2: fp32 [d]; out: out_dtype [T, d].
+ * hidden: caller-provided scratch of T*F elements of the input dtype.
+ * Replaces fused_ffn(h, w1, b1, w2, b2) -- tjkernels/kernels/__init__.py:80-89
+ * and tjkernels/kernels/ffn.py:113-128.
+ */
+int tjb_ffn(const void* h, const void* w1, const float* b1, const void* w2,
+            const float* b2, void* out, void* hidden, int T, int d, int F,
+            int in_dtype, int out_dtype, tjb_stream_t stream);
+
+/*
+ * Classify a padding mask on the device, with no host synchronisation.
+ * mask: uint8/bool [B, S].  lengths[b] = number of valid positions in row b.
+ * *flags = 0 when every row is a prefix (positions < lengths[b]) and
+ * TJB_ERR_NON_PREFIX_MASK otherwise.
+ * Replaces Engine._mask_mode (tjkernels/engine.py:131-158), which needed one
+ * or two host synchronisations per distinct mask tensor.
+ */
+int tjb_mask_lengths(const uint8_t* mask, int B, int S, int32_t* lengths,
+                     int32_t* flags, tjb_stream_t stream);
+
+/*
+ * Device status word of the current device: TJB_OK, or the first error a
+ * kernel recorded (TJB_ERR_DEVICE_TIMEOUT).  Synchronises the device.  When
+ * clear != 0 the word is reset to TJB_OK afterwards.
+ * No counterpart in the reference (its Triton kernels have no device-side
+ * waits).
+ */
+int tjb_device_status(int clear);
+
+/*
+ * Self-test of the bounded device-side wait: one thread spins on *flag
+ * (device int32) until it becomes non-zero or timeout_ns elapses; on timeout
+ * it records TJB_ERR_DEVICE_TIMEOUT in the device status word.
+ * No counterpart in the reference; used to test failure detection without
+ * faulting the GPU.
+ */
+int tjb_selftest_wait(const int32_t* flag, int64_t timeout_ns, tjb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TJB200_H */

@@ -1,0 +1,120 @@
+"""Host-side checks that need no GPU: the C-ABI library loads and exports
+every symbol the header declares; argument validation answers without a
+device; plan dispatch; and the engine refuses to fall back to the CPU."""
+
+import json
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "tjb200.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^(?:int|const char\*)\s+(tjb_\w+)\(", text, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    from tjkernels import _lib
+    names = declared_symbols()
+    assert len(names) >= 9
+    handle = _lib.load()
+    for name in names:
+        assert hasattr(handle, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    assert handle.tjb_version() >= 100
+
+
+def test_status_strings():
+    from tjkernels import _lib
+    lib = _lib.lib()
+    assert lib.tjb_status_string(0) == b"ok"
+    assert b"timed out" in lib.tjb_status_string(7)
+    assert lib.tjb_status_string(12345) == b"unknown status"
+
+
+def test_argument_validation_without_device():
+    """Null pointers and bad shapes are rejected before any device work."""
+    from tjkernels import _lib
+    lib = _lib.lib()
+    assert lib.tjb_add_layernorm(None, None, None, None, None, None, 4, 8, 1e-5, 0, 0,
+                                 None, None) == 1
+    assert lib.tjb_gemm_bias(None, None, None, None, 1, 8, 8, 8, 8, 8, 2, 2, 0, None) == 1
+    assert lib.tjb_flash_fwd(None, None, 1, 1, 1, 64, 1.0, 1, None, None, None, 2, None) == 1
+    # Non-null but shape-invalid arguments: K not a multiple of 8.
+    fake = 1 << 20
+    assert lib.tjb_gemm_bias(fake, fake, None, fake, 1, 8, 7, 8, 8, 8, 2, 2, 0, None) == 2
+    # Unsupported head dim.
+    assert lib.tjb_flash_fwd(fake, fake, 1, 1, 1, 48, 1.0, 1, None, None, None, 2, None) == 2
+    # Unsupported dtype (fp32 tensor-core input).
+    assert lib.tjb_gemm_bias(fake, fake, None, fake, 1, 8, 8, 8, 8, 8, 0, 0, 0, None) == 4
+
+
+def test_kernel_error_carries_status():
+    from tjkernels import _lib
+    with pytest.raises(_lib.KernelError) as info:
+        _lib.check(3, "probe")
+    assert info.value.status == 3 and "aligned" in str(info.value)
+
+
+def test_plan_roundtrip_and_env(tmp_path, monkeypatch):
+    from tjkernels import plans
+    p = plans.Plan(compute_dtype=torch.float16, delta_dtype=torch.bfloat16, cuda_graph=False,
+                   label="x")
+    assert plans.Plan.from_json(json.loads(json.dumps(p.to_json()))) == p
+    key = plans.shape_key(2, 128, 512, 8, 2048, 4, True, torch.float32)
+    assert key == "b2_s128_d512_h8_f2048_l4_causal_float32"
+    path = tmp_path / "plans.json"
+    plans.save_plans({key: p}, path)
+    assert json.loads(path.read_text())[key]["compute_dtype"] == "float16"
+    dev = torch.device("cuda")
+    monkeypatch.setenv("TJ_IGNORE_PLANS", "1")
+    plans._cache = None
+    base = plans.select_plan(2, 128, 512, 8, 2048, 4, True, torch.float32, dev)
+    assert base.compute_dtype == torch.bfloat16 and base.cuda_graph
+    big = plans.select_plan(64, 2048, 4096, 32, 16384, 12, True, torch.float32, dev)
+    assert not big.cuda_graph  # 2 GB input: graph copy-in/clone-out not free
+    monkeypatch.setenv("TJ_NO_GRAPH", "1")
+    monkeypatch.setenv("TJ_COMPUTE_DTYPE", "float16")
+    forced = plans.select_plan(2, 128, 512, 8, 2048, 4, True, torch.float32, dev)
+    assert not forced.cuda_graph and forced.compute_dtype == torch.float16
+    plans.set_override(p)
+    try:
+        assert plans.select_plan(1, 1, 1, 1, 1, 1, True, torch.float32, dev) is p
+    finally:
+        plans.set_override(None)
+        plans._cache = None
+
+
+def test_no_cpu_fallback():
+    from tjkernels import plans
+    with pytest.raises(RuntimeError):
+        plans.default_plan(1, 8, 128, 2, 128, 1, True, torch.float32, torch.device("cpu"))
+    import tjkernels.kernels as K
+    with pytest.raises(RuntimeError):
+        K.gemm_bias(torch.zeros(8, 8, dtype=torch.bfloat16),
+                    torch.zeros(8, 8, dtype=torch.bfloat16), None)
+
+
+def test_tj_disable_runs_baseline(monkeypatch):
+    """TJ_DISABLE=1 routes the hook to the baseline forward (engine.py:322)."""
+    import tjkernels
+    from oracle.model import ModelConfig, ReferenceModel, generate_case
+
+    class Optimized(ReferenceModel):
+        def forward(self, x, valid_token_mask=None):
+            return tjkernels.forward(self, x, valid_token_mask)
+
+    cfg = ModelConfig(1, 16, 128, 2, 128, 1, True)
+    torch.manual_seed(0)
+    model = Optimized(cfg).eval()
+    x, m = generate_case(cfg, 0, 0.3)
+    monkeypatch.setenv("TJ_DISABLE", "1")
+    with torch.no_grad():
+        out = model(x, m)
+        ref = ReferenceModel.forward(model, x, m)
+    assert torch.equal(out, ref)

@@ -1,0 +1,232 @@
+"""Kernel-level parity of the sm_100a library against fp32/fp64 torch
+references (modelled on the reference's bench/test_flash.py:36-48, which
+checks flash attention against an fp64 reference).  Calls go through the C
+ABI via the tjkernels.kernels facade."""
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _need_gpu():
+    if not torch.cuda.is_available():
+        pytest.fail("GPU tests need a CUDA device")
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+
+
+def K():
+    import tjkernels.kernels as kernels
+    return kernels
+
+
+# ------------------------------------------------------------------ LayerNorm
+
+@pytest.mark.parametrize("rows,d", [(1, 128), (37, 96), (256, 512), (1000, 768),
+                                    (513, 1024), (64, 4096), (8, 8192)])
+@pytest.mark.parametrize("delta_dtype", [None, torch.float32, torch.bfloat16, torch.float16])
+def test_add_layernorm(rows, d, delta_dtype):
+    g = torch.Generator(device=DEV).manual_seed(rows * 7 + d)
+    res = torch.randn(rows, d, device=DEV, generator=g) * 3 + 0.5
+    delta = None if delta_dtype is None else \
+        torch.randn(rows, d, device=DEV, generator=g).to(delta_dtype)
+    w = torch.randn(d, device=DEV, generator=g)
+    b = torch.randn(d, device=DEV, generator=g)
+    x = res + (0 if delta is None else delta.float())
+    ref = F.layer_norm(x, (d,), w, b, 1e-5)
+    new_res, out = K().fused_add_layernorm(res, delta, w, b, 1e-5, out_dtype=torch.float32)
+    assert (out - ref).abs().max().item() < 1e-4
+    if delta is not None:
+        assert torch.equal(new_res, x)
+    _, out16 = K().fused_add_layernorm(res, delta, w, b, 1e-5, out_dtype=torch.bfloat16)
+    assert ((out16.float() - ref).abs() <= 1e-2 * ref.abs() + 1e-2).all()
+
+
+def test_add_layernorm_row_mask_and_inplace():
+    rows, d = 300, 1024
+    res = torch.randn(rows, d, device=DEV)
+    delta = torch.randn(rows, d, device=DEV)
+    w, b = torch.randn(d, device=DEV), torch.randn(d, device=DEV)
+    mask = (torch.rand(rows, device=DEV) > 0.4).to(torch.uint8)
+    expect_res = res + delta
+    ref = F.layer_norm(expect_res, (d,), w, b, 1e-5)
+    got_res, out = K().fused_add_layernorm(res, delta, w, b, 1e-5, out_dtype=torch.float32,
+                                           row_mask=mask, residual_out=res)
+    assert got_res.data_ptr() == res.data_ptr()
+    assert torch.equal(res, expect_res)
+    keep = mask.bool()
+    assert (out[~keep] == 0).all()
+    assert (out[keep] - ref[keep]).abs().max().item() < 1e-4
+
+
+# ----------------------------------------------------------------------- GEMM
+
+GEMM_SHAPES = [(1, 64, 64), (64, 2304, 768), (100, 136, 96), (128, 256, 128), (256, 1536, 512),
+               (300, 1024, 1024), (1000, 3072, 1024), (2048, 1024, 4096), (4096, 4096, 1024)]
+
+
+@pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_gemm_bias(m, n, k, dtype):
+    g = torch.Generator(device=DEV).manual_seed(m + n + k)
+    a = torch.randn(m, k, device=DEV, generator=g).to(dtype)
+    w = (torch.randn(n, k, device=DEV, generator=g) / math.sqrt(k)).to(dtype)
+    bias = torch.randn(n, device=DEV, generator=g)
+    ref = a.double() @ w.double().T + bias.double()
+    out32 = K().gemm_bias(a, w, bias, out_dtype=torch.float32)
+    scale = ref.abs().max().item() + 1e-6
+    assert (out32.double() - ref).abs().max().item() <= 1e-5 * scale + 1e-5
+    out16 = K().gemm_bias(a, w, bias)
+    assert out16.dtype == dtype
+    tol = 2 ** -7 if dtype == torch.bfloat16 else 2 ** -10
+    assert ((out16.double() - ref).abs() <= tol * ref.abs() + 1e-3 * scale).all()
+
+
+@pytest.mark.parametrize("m,n,k", [(200, 512, 256), (1024, 4096, 1024)])
+def test_gemm_gelu(m, n, k):
+    a = torch.randn(m, k, device=DEV).bfloat16()
+    w = (torch.randn(n, k, device=DEV) / math.sqrt(k)).bfloat16()
+    bias = torch.randn(n, device=DEV)
+    ref = F.gelu(a.double() @ w.double().T + bias.double(), approximate="none")
+    out = K().gemm_bias(a, w, bias, act=K().ACT_GELU, out_dtype=torch.float32)
+    assert (out.double() - ref).abs().max().item() < 1e-4
+
+
+def test_gemm_no_bias_and_errors():
+    a = torch.randn(128, 64, device=DEV).bfloat16()
+    w = torch.randn(64, 64, device=DEV).bfloat16()
+    out = K().gemm_bias(a, w, None, out_dtype=torch.float32)
+    assert (out.double() - a.double() @ w.double().T).abs().max().item() < 1e-3
+    from tjkernels._lib import KernelError
+    with pytest.raises(KernelError):  # N not a multiple of 8
+        K().gemm_bias(a, torch.randn(60, 64, device=DEV).bfloat16(), None)
+
+
+# ------------------------------------------------------------------ attention
+
+def attn_reference(qkv, causal, lengths=None, key_mask=None):
+    """fp64 attention over [B,S,3,H,hd] -> [B*S, H*hd] (bench/test_flash.py:36-48)."""
+    b, s, _, h, hd = qkv.shape
+    q = qkv[:, :, 0].transpose(1, 2).double()
+    k = qkv[:, :, 1].transpose(1, 2).double()
+    v = qkv[:, :, 2].transpose(1, 2).double()
+    scores = (q @ k.transpose(-2, -1)) * hd ** -0.5
+    if causal:
+        scores = scores.masked_fill(
+            torch.ones(s, s, dtype=torch.bool, device=qkv.device).triu(1), float("-inf"))
+    if lengths is not None:
+        keep = torch.arange(s, device=qkv.device)[None, :] < lengths[:, None]
+        scores = scores.masked_fill(~keep[:, None, None, :], float("-inf"))
+    if key_mask is not None:
+        scores = scores.masked_fill(~key_mask.bool()[:, None, None, :], float("-inf"))
+    probs = torch.softmax(scores, dim=-1)
+    probs = torch.nan_to_num(probs, nan=0.0)
+    return (probs @ v).transpose(1, 2).reshape(b * s, h * hd)
+
+
+ATTN_CASES = [(1, 1, 1, 64), (2, 37, 2, 64), (2, 128, 4, 64), (1, 200, 2, 128),
+              (2, 256, 2, 64), (1, 1000, 2, 64), (1, 513, 1, 128), (2, 2048, 2, 64)]
+
+
+@pytest.mark.parametrize("b,s,h,hd", ATTN_CASES)
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_flash_dense(b, s, h, hd, causal, dtype):
+    g = torch.Generator(device=DEV).manual_seed(b * 1000 + s + h + hd)
+    qkv = torch.randn(b, s, 3, h, hd, device=DEV, generator=g).to(dtype)
+    out = K().flash_attention(qkv, h, causal=causal)
+    ref = attn_reference(qkv, causal)
+    err = (out.double() - ref).abs().max().item()
+    assert err < (2e-2 if dtype == torch.bfloat16 else 4e-3), err
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("hd", [64, 128])
+def test_flash_prefix_lengths(causal, hd):
+    b, s, h = 4, 700, 2
+    qkv = torch.randn(b, s, 3, h, hd, device=DEV).bfloat16()
+    lengths = torch.tensor([700, 1, 129, 384], dtype=torch.int32, device=DEV)
+    mask = torch.arange(s, device=DEV)[None, :] < lengths[:, None]
+    lens, flags = K().mask_lengths(mask)
+    assert torch.equal(lens, lengths) and int(flags.item()) == 0
+    out = K().flash_attention(qkv, h, causal=causal, lengths=lens,
+                              key_mask=mask.to(torch.uint8), mask_flags=flags)
+    ref = attn_reference(qkv, causal, lengths=lengths)
+    valid = mask.reshape(-1)
+    assert (out.double()[valid] - ref[valid]).abs().max().item() < 2e-2
+    # Query tiles wholly past the length are skipped and written as zeros.
+    rows = out.view(b, s, -1)
+    assert (rows[1, 128:] == 0).all()
+    assert torch.isfinite(out).all()
+
+
+def test_flash_general_key_mask():
+    b, s, h, hd = 2, 300, 2, 64
+    qkv = torch.randn(b, s, 3, h, hd, device=DEV).bfloat16()
+    key_mask = (torch.rand(b, s, device=DEV) > 0.3)
+    key_mask[:, 0] = True
+    lens, flags = K().mask_lengths(key_mask)
+    assert int(flags.item()) != 0
+    out = K().flash_attention(qkv, h, causal=True, lengths=lens,
+                              key_mask=key_mask.to(torch.uint8), mask_flags=flags)
+    ref = attn_reference(qkv, True, key_mask=key_mask)
+    assert (out.double() - ref).abs().max().item() < 2e-2
+    assert torch.isfinite(out).all()
+
+
+def test_flash_unsupported_head_dim():
+    from tjkernels._lib import KernelError
+    qkv = torch.randn(1, 64, 3, 4, 32, device=DEV).bfloat16()
+    with pytest.raises(KernelError):
+        K().flash_attention(qkv, 4)
+
+
+# ------------------------------------------------------------------------ FFN
+
+@pytest.mark.parametrize("t,d,f", [(1, 128, 512), (256, 512, 2048), (1000, 1024, 4096)])
+def test_ffn(t, d, f):
+    h = torch.randn(t, d, device=DEV).bfloat16()
+    w1 = (torch.randn(f, d, device=DEV) / math.sqrt(d)).bfloat16()
+    w2 = (torch.randn(d, f, device=DEV) / math.sqrt(f)).bfloat16()
+    b1, b2 = torch.randn(f, device=DEV), torch.randn(d, device=DEV)
+    hidden = F.gelu(h.double() @ w1.double().T + b1.double(), approximate="none")
+    ref = hidden.bfloat16().double() @ w2.double().T + b2.double()
+    out = K().fused_ffn(h, w1, b1, w2, b2, out_dtype=torch.float32)
+    assert (out.double() - ref).abs().max().item() < 2e-2
+
+
+# ------------------------------------------------------------- mask / status
+
+def test_mask_lengths_cases():
+    m = torch.zeros(3, 50, dtype=torch.bool, device=DEV)
+    m[0, :50] = True
+    m[1, :7] = True
+    lens, flags = K().mask_lengths(m)
+    assert lens.tolist() == [50, 7, 0] and int(flags.item()) == 0
+    m[2, 10] = True  # 0 -> 1 step: not a prefix
+    lens, flags = K().mask_lengths(m)
+    assert lens.tolist() == [50, 7, 1] and int(flags.item()) != 0
+
+
+def test_bounded_wait_times_out_and_reports():
+    from tjkernels import _lib
+    assert K().device_status(clear=True) == 0
+    never = torch.zeros(1, dtype=torch.int32, device=DEV)
+    _lib.check(_lib.lib().tjb_selftest_wait(never.data_ptr(), 50_000_000,
+                                            torch.cuda.current_stream().cuda_stream), "wait")
+    assert K().device_status(clear=True) == 7  # TJB_ERR_DEVICE_TIMEOUT
+    assert K().device_status() == 0
+    ready = torch.ones(1, dtype=torch.int32, device=DEV)
+    _lib.check(_lib.lib().tjb_selftest_wait(ready.data_ptr(), 50_000_000,
+                                            torch.cuda.current_stream().cuda_stream), "wait")
+    assert K().device_status() == 0
+    # The context is still usable afterwards.
+    x = torch.randn(128, 64, device=DEV).bfloat16()
+    assert torch.isfinite(K().gemm_bias(x, x[:64], None)).all()

@@ -1,0 +1,348 @@
+// gemm.cu -- C = act(A * B^T + bias) on the 5th-generation tensor cores.
+//
+// Persistent, warp-specialised kernel, one CTA per SM (192 threads):
+//   warp 0      TMA producer: streams 128x64 A tiles and BNx64 B tiles
+//               (128-byte swizzle) into a kStages-deep shared-memory ring.
+//   warp 1      allocates tensor memory; one lane issues tcgen05.mma
+//               (M=128, N=BN, K=16) into a double-buffered fp32 accumulator
+//               in TMEM and commits stage/accumulator completion to mbarriers.
+//   warps 2..5  epilogue: tcgen05.ld the accumulator (one TMEM lane = one
+//               output row per thread), add bias, optional erf-GELU, convert,
+//               store; then hand the accumulator buffer back to the MMA warp.
+// The epilogue of tile i overlaps the main loop of tile i+1.  Output tiles are
+// visited in groups of 16 M-blocks so the CTAs resident at one time share
+// both A rows and B columns in L2.
+#include <mutex>
+
+#include "common.cuh"
+
+namespace tjb {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // 64 x 16-bit = one 128-byte swizzle row
+constexpr int kGroupM = 16;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr uint32_t kABytes = kBM * kBK * 2;
+  static constexpr uint32_t kBBytes = BN * kBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators; 128/256/512
+  static constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + 256;
+};
+
+struct GemmArgs {
+  const float* bias;
+  void* C;
+  int M, N, K, ldc;
+  int out_dtype;
+  int act;
+  uint32_t idesc;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m_blk, int& n_blk) {
+  const int per_group = kGroupM * num_n;
+  const int group = t / per_group;
+  const int first_m = group * kGroupM;
+  const int gsize = min(num_m - first_m, kGroupM);
+  const int r = t - group * per_group;
+  m_blk = first_m + r % gsize;
+  n_blk = r / gsize;
+}
+
+// Epilogue for one 32-column slice of one row: bias, activation, store.
+__device__ __forceinline__ void store_slice(const GemmArgs& a, int row, int col0,
+                                            const uint32_t (&acc)[32]) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(acc[i]);
+  const bool full = col0 + 32 <= a.N;
+  if (a.bias != nullptr) {
+    if (full) {
+      const float4* b4 = reinterpret_cast<const float4*>(a.bias + col0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 bb = __ldg(b4 + i);
+        v[4 * i] += bb.x;
+        v[4 * i + 1] += bb.y;
+        v[4 * i + 2] += bb.z;
+        v[4 * i + 3] += bb.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < a.N) v[i] += __ldg(a.bias + col0 + i);
+    }
+  }
+  if (a.act == 1) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+  }
+  if (row >= a.M) return;
+  if (a.out_dtype == TJB_F32) {
+    float* dst = static_cast<float*>(a.C) + static_cast<int64_t>(row) * a.ldc + col0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (full || col0 + 4 * j < a.N)
+        reinterpret_cast<float4*>(dst)[j] =
+            make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  } else {
+    uint32_t p[16];
+    if (a.out_dtype == TJB_BF16) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) p[i] = Pack2<__nv_bfloat16>::pack(v[2 * i], v[2 * i + 1]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) p[i] = Pack2<__half>::pack(v[2 * i], v[2 * i + 1]);
+    }
+    uint16_t* dst = static_cast<uint16_t*>(a.C) + static_cast<int64_t>(row) * a.ldc + col0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (full || col0 + 8 * j < a.N)
+        reinterpret_cast<uint4*>(dst)[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const GemmArgs args) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int kStages = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kStages * Cfg::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + kStages * Cfg::kBBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (args.M + kBM - 1) / kBM;
+  const int num_n = (args.N + BN - 1) / BN;
+  const int num_k = (args.K + kBK - 1) / kBK;
+  const int num_tiles = num_m * num_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      int stage = 0;
+      uint32_t phase = 0, issued = 0, issued_parity = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int m_blk, n_blk;
+        tile_coords(t, num_m, num_n, m_blk, n_blk);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          tma_load_2d(sA + stage * Cfg::kABytes, &tmA, &full[stage], kb * kBK, m_blk * kBM);
+          tma_load_2d(sB + stage * Cfg::kBBytes, &tmB, &full[stage], kb * kBK, n_blk * BN);
+          issued |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Every load this thread issued has landed before the CTA may exit.
+      for (int s = 0; s < kStages; ++s)
+        if ((issued >> s) & 1u) mbar_wait_drain(&full[s], (issued_parity >> s) & 1u);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- MMA issuer
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * Cfg::kABytes);
+          const uint32_t b0 = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            umma_ss(d_tmem, sdesc_sw128(a0 + k * 32, 16, 1024), sdesc_sw128(b0 + k * 32, 16, 1024),
+                    args.idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      // All issued MMAs retire before tensor memory is released.
+      umma_commit(drain);
+      mbar_wait_drain(drain, 0);
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue
+    const int quad = warp & 3;  // TMEM lanes this warp may access
+    const int r_in_tile = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      int m_blk, n_blk;
+      tile_coords(t, num_m, num_n, m_blk, n_blk);
+      bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const int row = m_blk * kBM + r_in_tile;
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c * 32, r);
+        tmem_ld_wait(r);
+        const int col0 = n_blk * BN + c * 32;
+        if (col0 < args.N) store_slice(args, row, col0, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+std::mutex g_attr_mu;
+bool g_attr_done[64][3];
+
+template <int BN>
+int launch_gemm(const void* A, const void* B, const GemmArgs& args, int lda, int ldb, bool bf16,
+                cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int slot = BN == 256 ? 0 : (BN == 128 ? 1 : 2);
+  {
+    std::lock_guard<std::mutex> lock(g_attr_mu);
+    if (dev < 64 && !g_attr_done[dev][slot]) {
+      if (cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(Cfg::kSmemBytes)) != cudaSuccess)
+        return TJB_ERR_LAUNCH;
+      g_attr_done[dev][slot] = true;
+    }
+  }
+  CUtensorMap tmA, tmB;
+  const uint64_t dimA[2] = {static_cast<uint64_t>(args.K), static_cast<uint64_t>(args.M)};
+  const uint64_t strA[1] = {static_cast<uint64_t>(lda) * 2};
+  const uint32_t boxA[2] = {kBK, kBM};
+  const uint64_t dimB[2] = {static_cast<uint64_t>(args.K), static_cast<uint64_t>(args.N)};
+  const uint64_t strB[1] = {static_cast<uint64_t>(ldb) * 2};
+  const uint32_t boxB[2] = {kBK, static_cast<uint32_t>(BN)};
+  int st = make_tmap_16bit(&tmA, 2, A, dimA, strA, boxA, bf16);
+  if (st != TJB_OK) return st;
+  st = make_tmap_16bit(&tmB, 2, B, dimB, strB, boxB, bf16);
+  if (st != TJB_OK) return st;
+  const int num_tiles = ((args.M + kBM - 1) / kBM) * ((args.N + BN - 1) / BN);
+  const int grid = num_tiles < num_sms() ? num_tiles : num_sms();
+  gemm_kernel<BN><<<grid, 192, Cfg::kSmemBytes, stream>>>(tmA, tmB, args);
+  return launch_status();
+}
+
+}  // namespace
+}  // namespace tjb
+
+extern "C" int tjb_gemm_bias(const void* A, const void* B, const float* bias, void* C, int M,
+                             int N, int K, int lda, int ldb, int ldc, int in_dtype, int out_dtype,
+                             int act, tjb_stream_t stream) {
+  using namespace tjb;
+  if (!A || !B || !C || M < 0 || N <= 0 || K <= 0) return TJB_ERR_INVALID_ARGUMENT;
+  if (in_dtype != TJB_F16 && in_dtype != TJB_BF16) return TJB_ERR_UNSUPPORTED_DTYPE;
+  if (out_dtype != TJB_F32 && out_dtype != in_dtype) return TJB_ERR_UNSUPPORTED_DTYPE;
+  if (act != 0 && act != 1) return TJB_ERR_INVALID_ARGUMENT;
+  if (K % 8 != 0 || N % 8 != 0 || lda < K || ldb < K || ldc < N) return TJB_ERR_BAD_SHAPE;
+  if (lda % 8 != 0 || ldb % 8 != 0 || ldc % 8 != 0) return TJB_ERR_BAD_ALIGNMENT;
+  if (!aligned16(A) || !aligned16(B) || !aligned16(C) || (bias && !aligned16(bias)))
+    return TJB_ERR_BAD_ALIGNMENT;
+  if (!device_ok()) return TJB_ERR_NO_DEVICE;
+  if (M == 0) return TJB_OK;
+  const bool bf16 = in_dtype == TJB_BF16;
+  GemmArgs args;
+  args.bias = bias;
+  args.C = C;
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.ldc = ldc;
+  args.out_dtype = out_dtype;
+  args.act = act;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int sms = num_sms();
+  const int mt = (M + kBM - 1) / kBM;
+  const long tiles256 = static_cast<long>(mt) * ((N + 255) / 256);
+  const long tiles128 = static_cast<long>(mt) * ((N + 127) / 128);
+  if (N >= 256 && tiles256 >= sms) {
+    args.idesc = idesc_f16(kBM, 256, bf16, false);
+    return launch_gemm<256>(A, B, args, lda, ldb, bf16, s);
+  }
+  if (N >= 128 && tiles128 >= sms / 2) {
+    args.idesc = idesc_f16(kBM, 128, bf16, false);
+    return launch_gemm<128>(A, B, args, lda, ldb, bf16, s);
+  }
+  args.idesc = idesc_f16(kBM, 64, bf16, false);
+  return launch_gemm<64>(A, B, args, lda, ldb, bf16, s);
+}

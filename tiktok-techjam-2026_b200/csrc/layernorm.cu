@@ -1,0 +1,177 @@
+// layernorm.cu -- fused residual-add + LayerNorm (HBM-bound).
+//
+// One row is owned by TPR threads (a warp for d <= 1024, four warps for
+// d <= 4096, eight for d <= 8192).  Each thread holds up to 8 float4 chunks
+// of the row in registers (chunk i of thread t covers columns
+// 4*(i*TPR + t) .. +3, so a warp's loads are 512 contiguous bytes), reduces
+// sum and centred sum of squares with shuffles (plus shared memory across
+// warps when TPR > 32), and writes the new residual and the normalised row
+// with 16-byte (fp32) or 8-byte (16-bit) vector stores.
+#include "common.cuh"
+
+namespace tjb {
+
+namespace {
+
+__device__ __forceinline__ float4 load_delta4(const void* delta, int dtype, int64_t idx) {
+  if (dtype == TJB_F32) {
+    return __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(delta) + idx));
+  }
+  const uint2 raw = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(delta) + idx));
+  float4 r;
+  if (dtype == TJB_BF16) {
+    const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+    const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+    const float2 a = __bfloat1622float2(lo), b = __bfloat1622float2(hi);
+    r = make_float4(a.x, a.y, b.x, b.y);
+  } else {
+    const __half2 lo = *reinterpret_cast<const __half2*>(&raw.x);
+    const __half2 hi = *reinterpret_cast<const __half2*>(&raw.y);
+    const float2 a = __half22float2(lo), b = __half22float2(hi);
+    r = make_float4(a.x, a.y, b.x, b.y);
+  }
+  return r;
+}
+
+__device__ __forceinline__ void store_out4(void* out, int dtype, int64_t idx, float4 y) {
+  if (dtype == TJB_F32) {
+    *reinterpret_cast<float4*>(static_cast<float*>(out) + idx) = y;
+    return;
+  }
+  uint2 raw;
+  if (dtype == TJB_BF16) {
+    raw.x = Pack2<__nv_bfloat16>::pack(y.x, y.y);
+    raw.y = Pack2<__nv_bfloat16>::pack(y.z, y.w);
+  } else {
+    raw.x = Pack2<__half>::pack(y.x, y.y);
+    raw.y = Pack2<__half>::pack(y.z, y.w);
+  }
+  *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + idx) = raw;
+}
+
+// Sum over the TPR threads that own one row.  Every thread of the block must
+// call it (it may use __syncthreads).
+template <int TPR>
+__device__ __forceinline__ float row_sum(float v, float* scratch) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if constexpr (TPR <= 32) {
+    return v;
+  } else {
+    constexpr int WPR = TPR / 32;  // warps per row
+    const int warp = threadIdx.x >> 5;
+    __syncthreads();  // scratch reuse across calls
+    if ((threadIdx.x & 31) == 0) scratch[warp] = v;
+    __syncthreads();
+    const int first = (warp / WPR) * WPR;
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < WPR; ++i) s += scratch[first + i];
+    return s;
+  }
+}
+
+constexpr int kBlock = 256;
+constexpr int kMaxChunks = 8;
+
+template <int TPR>
+__global__ void __launch_bounds__(kBlock) add_layernorm_kernel(
+    const float* res, const void* __restrict__ delta, float* res_out, void* out,
+    const float* __restrict__ w, const float* __restrict__ b, int64_t rows, int d, float eps,
+    int delta_dtype, int out_dtype, const uint8_t* __restrict__ row_mask) {
+  static_assert(TPR == 32 || TPR == 128 || TPR == 256, "threads per row");
+  constexpr int kRowsPerBlock = kBlock / TPR;
+  __shared__ float scratch[kBlock / 32];
+
+  const int t = threadIdx.x % TPR;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + threadIdx.x / TPR;
+  const bool active = row < rows;
+  const int64_t base = row * d;
+
+  float4 v[kMaxChunks];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int col = (i * TPR + t) * 4;
+    v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (active && col < d) {
+      v[i] = __ldg(reinterpret_cast<const float4*>(res + base + col));
+      if (delta != nullptr) {
+        const float4 dl = load_delta4(delta, delta_dtype, base + col);
+        v[i].x += dl.x;
+        v[i].y += dl.y;
+        v[i].z += dl.z;
+        v[i].w += dl.w;
+      }
+      sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    }
+  }
+  const float inv_d = 1.0f / static_cast<float>(d);
+  const float mean = row_sum<TPR>(sum, scratch) * inv_d;
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int col = (i * TPR + t) * 4;
+    if (active && col < d) {
+      const float a = v[i].x - mean, bb = v[i].y - mean, c = v[i].z - mean, e = v[i].w - mean;
+      sq += (a * a + bb * bb) + (c * c + e * e);
+    }
+  }
+  const float var = row_sum<TPR>(sq, scratch) * inv_d;
+  const float rstd = rsqrtf(var + eps);
+  if (!active) return;
+  const bool zero_row = row_mask != nullptr && row_mask[row] == 0;
+
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int col = (i * TPR + t) * 4;
+    if (col < d) {
+      if (res_out != nullptr) *reinterpret_cast<float4*>(res_out + base + col) = v[i];
+      float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (!zero_row) {
+        const float4 ww = __ldg(reinterpret_cast<const float4*>(w + col));
+        const float4 bb = __ldg(reinterpret_cast<const float4*>(b + col));
+        y.x = (v[i].x - mean) * rstd * ww.x + bb.x;
+        y.y = (v[i].y - mean) * rstd * ww.y + bb.y;
+        y.z = (v[i].z - mean) * rstd * ww.z + bb.z;
+        y.w = (v[i].w - mean) * rstd * ww.w + bb.w;
+      }
+      store_out4(out, out_dtype, base + col, y);
+    }
+  }
+}
+
+}  // namespace
+}  // namespace tjb
+
+extern "C" int tjb_add_layernorm(const float* res, const void* delta, float* res_out, void* out,
+                                 const float* w, const float* b, int64_t rows, int d, float eps,
+                                 int delta_dtype, int out_dtype, const uint8_t* row_mask,
+                                 tjb_stream_t stream) {
+  using namespace tjb;
+  if (!res || !out || !w || !b || rows < 0 || d <= 0) return TJB_ERR_INVALID_ARGUMENT;
+  if (d % 4 != 0 || d > 8192) return TJB_ERR_BAD_SHAPE;
+  if (delta_dtype < TJB_F32 || delta_dtype > TJB_BF16 || out_dtype < TJB_F32 ||
+      out_dtype > TJB_BF16)
+    return TJB_ERR_UNSUPPORTED_DTYPE;
+  if (!aligned16(res) || !aligned16(w) || !aligned16(b) || (res_out && !aligned16(res_out)) ||
+      (delta && (reinterpret_cast<uintptr_t>(delta) & 7u)) ||
+      (reinterpret_cast<uintptr_t>(out) & 7u))
+    return TJB_ERR_BAD_ALIGNMENT;
+  if (!device_ok()) return TJB_ERR_NO_DEVICE;
+  if (rows == 0) return TJB_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (d <= 1024) {
+    const int64_t grid = (rows + (kBlock / 32) - 1) / (kBlock / 32);
+    add_layernorm_kernel<32><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
+        res, delta, res_out, out, w, b, rows, d, eps, delta_dtype, out_dtype, row_mask);
+  } else if (d <= 4096) {
+    const int64_t grid = (rows + (kBlock / 128) - 1) / (kBlock / 128);
+    add_layernorm_kernel<128><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
+        res, delta, res_out, out, w, b, rows, d, eps, delta_dtype, out_dtype, row_mask);
+  } else {
+    add_layernorm_kernel<256><<<static_cast<unsigned>(rows), kBlock, 0, s>>>(
+        res, delta, res_out, out, w, b, rows, d, eps, delta_dtype, out_dtype, row_mask);
+  }
+  return launch_status();
+}

@@ -1,0 +1,195 @@
+// runtime.cu -- host-side runtime of libtjb200: status strings, the device
+// status word, SM-count cache, tensor-map encoding through the driver entry
+// point (no link-time dependency on libcuda), and two small device kernels:
+// padding-mask classification and the bounded-wait self-test.
+#include <mutex>
+
+#include "common.cuh"
+
+namespace tjb {
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+int g_sm_count[kMaxDevices] = {0};
+int g_cc_major[kMaxDevices] = {0};
+std::mutex g_dev_mu;
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+std::once_flag g_encode_once;
+
+void load_encode() {
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+          cudaSuccess &&
+      q == cudaDriverEntryPointSuccess) {
+    g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+}
+
+int current_device_cached() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  if (g_sm_count[dev] == 0) {
+    int sms = 0, major = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    g_sm_count[dev] = sms > 0 ? sms : 1;
+    g_cc_major[dev] = major;
+  }
+  return dev;
+}
+
+}  // namespace
+
+int num_sms() {
+  int dev = current_device_cached();
+  return dev < 0 ? 1 : g_sm_count[dev];
+}
+
+bool device_ok() {
+  int dev = current_device_cached();
+  return dev >= 0 && g_cc_major[dev] == 10;
+}
+
+int make_tmap_16bit(CUtensorMap* map, int rank, const void* base, const uint64_t* dims,
+                    const uint64_t* strides_bytes, const uint32_t* box, bool bf16) {
+  std::call_once(g_encode_once, load_encode);
+  if (g_encode == nullptr) return TJB_ERR_TENSOR_MAP;
+  cuuint64_t gdim[5];
+  cuuint64_t gstride[4];
+  cuuint32_t bdim[5];
+  cuuint32_t estride[5];
+  for (int i = 0; i < rank; ++i) {
+    gdim[i] = dims[i];
+    bdim[i] = box[i];
+    estride[i] = 1;
+    if (i > 0) gstride[i - 1] = strides_bytes[i - 1];
+  }
+  CUresult r = g_encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        static_cast<cuuint32_t>(rank), const_cast<void*>(base), gdim, gstride,
+                        bdim, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TJB_OK : TJB_ERR_TENSOR_MAP;
+}
+
+// ------------------------------------------------------------ mask lengths
+// One CTA walks every row: lengths[b] = popcount of row b; a row is a prefix
+// mask iff it has no 0 -> 1 step.
+__global__ void __launch_bounds__(1024) mask_lengths_kernel(const uint8_t* __restrict__ mask,
+                                                            int B, int S,
+                                                            int32_t* __restrict__ lengths,
+                                                            int32_t* __restrict__ flags) {
+  __shared__ int s_count[32];
+  __shared__ int s_step[32];
+  int any_step = 0;
+  for (int b = 0; b < B; ++b) {
+    const uint8_t* row = mask + static_cast<int64_t>(b) * S;
+    int count = 0, step = 0;
+    for (int j = threadIdx.x; j < S; j += blockDim.x) {
+      const int v = row[j] != 0;
+      count += v;
+      if (j > 0 && v && row[j - 1] == 0) step = 1;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      count += __shfl_xor_sync(0xffffffffu, count, o);
+      step |= __shfl_xor_sync(0xffffffffu, step, o);
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+      s_count[warp] = count;
+      s_step[warp] = step;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      const int nw = (blockDim.x + 31) >> 5;
+      count = lane < nw ? s_count[lane] : 0;
+      step = lane < nw ? s_step[lane] : 0;
+      for (int o = 16; o > 0; o >>= 1) {
+        count += __shfl_xor_sync(0xffffffffu, count, o);
+        step |= __shfl_xor_sync(0xffffffffu, step, o);
+      }
+      if (lane == 0) {
+        lengths[b] = count;
+        any_step |= step;
+      }
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *flags = any_step ? TJB_ERR_NON_PREFIX_MASK : 0;
+}
+
+// --------------------------------------------------------- bounded-wait test
+__global__ void selftest_wait_kernel(const int32_t* flag, int64_t timeout_ns) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const volatile int32_t* f = flag;
+  const uint64_t t0 = globaltimer();
+  while (*f == 0) {
+    if (globaltimer() - t0 > static_cast<uint64_t>(timeout_ns)) {
+      record_status(TJB_ERR_DEVICE_TIMEOUT);
+      return;
+    }
+    __nanosleep(1000);
+  }
+}
+
+}  // namespace tjb
+
+// ==================================================================== C ABI
+extern "C" {
+
+int tjb_version(void) { return 100; }
+
+const char* tjb_status_string(int status) {
+  switch (status) {
+    case TJB_OK: return "ok";
+    case TJB_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case TJB_ERR_BAD_SHAPE: return "shape outside the kernel contract";
+    case TJB_ERR_BAD_ALIGNMENT: return "pointer or pitch not 16-byte aligned";
+    case TJB_ERR_UNSUPPORTED_DTYPE: return "unsupported dtype";
+    case TJB_ERR_LAUNCH: return "CUDA launch error";
+    case TJB_ERR_TENSOR_MAP: return "tensor map encoding failed";
+    case TJB_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    case TJB_ERR_NO_DEVICE: return "no sm_100 device is current";
+    case TJB_ERR_NON_PREFIX_MASK: return "padding mask is not a prefix mask";
+    default: return "unknown status";
+  }
+}
+
+int tjb_device_status(int clear) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return TJB_ERR_LAUNCH;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, tjb::g_device_status, sizeof(int)) != cudaSuccess)
+    return TJB_ERR_LAUNCH;
+  if (clear) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(tjb::g_device_status, &zero, sizeof(int)) != cudaSuccess)
+      return TJB_ERR_LAUNCH;
+  }
+  return v;
+}
+
+int tjb_mask_lengths(const uint8_t* mask, int B, int S, int32_t* lengths, int32_t* flags,
+                     tjb_stream_t stream) {
+  if (!mask || !lengths || !flags || B <= 0 || S <= 0) return TJB_ERR_INVALID_ARGUMENT;
+  if (!tjb::device_ok()) return TJB_ERR_NO_DEVICE;
+  tjb::mask_lengths_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      mask, B, S, lengths, flags);
+  return tjb::launch_status();
+}
+
+int tjb_selftest_wait(const int32_t* flag, int64_t timeout_ns, tjb_stream_t stream) {
+  if (!flag || timeout_ns <= 0) return TJB_ERR_INVALID_ARGUMENT;
+  if (!tjb::device_ok()) return TJB_ERR_NO_DEVICE;
+  tjb::selftest_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(flag,
+                                                                                  timeout_ns);
+  return tjb::launch_status();
+}
+
+}  // extern "C"

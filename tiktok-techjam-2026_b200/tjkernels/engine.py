@@ -1,0 +1,202 @@
+"""Execution engine: packs weights once, then runs the forward on sm_100a.
+
+Same public surface and contract as the reference's ``tjkernels/engine.py``:
+``forward(module, x, valid_token_mask)`` (:317-324), ``get_engine`` (:303-309),
+``reset_engines`` (:312-314), an ``Engine`` that reads the parameters off the
+baseline module instead of owning them (:1-7, :58-79), packs them per plan
+(:83-127), and runs the per-layer loop with the deferred residual (:205-269),
+optionally replayed as a CUDA graph (:273-300).
+
+Per layer (T = B*S tokens, residual stream fp32 [T, d]):
+
+    res, h  = add_layernorm(res, pending, ln1)      # pending = last FFN delta
+    qkv     = gemm(h, Wqkv) + bqkv                   # [T, 3d] -> [B,S,3,H,hd]
+    ctx     = attention(qkv)                         # [T, d], causal, in place
+    attn    = gemm(ctx, Wo) + bo                     # delta (fp32 by default)
+    res, h2 = add_layernorm(res, attn, ln2)
+    pending = ffn(h2)                                # delta
+    out     = add_layernorm(res, pending, final_ln)  # padded rows -> exact 0
+
+Padding masks are classified on the device (``tjb_mask_lengths``): no host
+synchronisation at all, unlike the reference's memoised ``.item()`` calls
+(:131-158).  A prefix mask lets attention skip query tiles past a sequence's
+length and stop keys at it; any other mask is applied key by key inside the
+attention kernel (the reference routed that case to SDPA with a bias).
+Padded rows never influence valid rows (row-wise ops, masked keys), so they
+are zeroed once, by the final LayerNorm.
+"""
+
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Tuple
+
+import torch
+
+from .graphs import GraphCache
+from .plans import Plan, select_plan
+from . import kernels as K
+
+
+@dataclass
+class LayerWeights:
+    """Packed weights of one block, in nn.Linear ``[out, in]`` layout."""
+
+    ln1_w: torch.Tensor
+    ln1_b: torch.Tensor
+    ln1_eps: float
+    wqkv: torch.Tensor   # [3d, d]  rows: q | k | v
+    bqkv: torch.Tensor   # [3d] fp32
+    wo: torch.Tensor     # [d, d]
+    bo: torch.Tensor     # [d] fp32
+    ln2_w: torch.Tensor
+    ln2_b: torch.Tensor
+    ln2_eps: float
+    w1: torch.Tensor     # [F, d]
+    b1: torch.Tensor     # [F] fp32
+    w2: torch.Tensor     # [d, F]
+    b2: torch.Tensor     # [d] fp32
+
+
+class Engine:
+    def __init__(self, module: torch.nn.Module) -> None:
+        cfg = module.config
+        param = next(module.parameters())
+        self.device = param.device
+        self.dtype = param.dtype
+        self.d_model = cfg.d_model
+        self.num_heads = cfg.num_heads
+        self.head_dim = cfg.d_model // cfg.num_heads
+        self.ffn_dim = cfg.ffn_dim
+        self.num_layers = cfg.num_layers
+        self.causal = cfg.causal
+        self.scale = self.head_dim ** -0.5
+
+        self.plan: Optional[Plan] = None
+        self._plan_cache: Dict[Tuple[int, int], Plan] = {}
+        self._built_for: Optional[Tuple] = None
+        self.layers: List[LayerWeights] = []
+        self.final_ln: Optional[Tuple[torch.Tensor, torch.Tensor, float]] = None
+        self._module = module
+        self._graphs = GraphCache()
+
+    # ---------------------------------------------------------------- weights
+
+    def _build(self, plan: Plan) -> None:
+        """Pack weights for ``plan``; once per (compute dtype, model dtype, device)."""
+        key = (plan.compute_dtype, self.dtype, self.device)
+        if self._built_for == key:
+            return
+        cdt = plan.compute_dtype
+        layers: List[LayerWeights] = []
+        with torch.no_grad():
+            for block in self._module.layers:
+                attn = block.attention
+                wqkv = torch.cat([attn.q_proj.weight, attn.k_proj.weight, attn.v_proj.weight],
+                                 dim=0).to(cdt).contiguous()
+                bqkv = torch.cat([attn.q_proj.bias, attn.k_proj.bias, attn.v_proj.bias],
+                                 dim=0).float().contiguous()
+                layers.append(LayerWeights(
+                    ln1_w=block.norm1.weight.float().contiguous(),
+                    ln1_b=block.norm1.bias.float().contiguous(),
+                    ln1_eps=block.norm1.eps,
+                    wqkv=wqkv,
+                    bqkv=bqkv,
+                    wo=attn.out_proj.weight.to(cdt).contiguous(),
+                    bo=attn.out_proj.bias.float().contiguous(),
+                    ln2_w=block.norm2.weight.float().contiguous(),
+                    ln2_b=block.norm2.bias.float().contiguous(),
+                    ln2_eps=block.norm2.eps,
+                    w1=block.ffn_in.weight.to(cdt).contiguous(),
+                    b1=block.ffn_in.bias.float().contiguous(),
+                    w2=block.ffn_out.weight.to(cdt).contiguous(),
+                    b2=block.ffn_out.bias.float().contiguous(),
+                ))
+            fn = self._module.final_norm
+            self.final_ln = (fn.weight.float().contiguous(), fn.bias.float().contiguous(),
+                             fn.eps)
+        self.layers = layers
+        self._built_for = key
+        self._graphs.clear()
+
+    # ---------------------------------------------------------------- compute
+
+    def _forward_impl(self, x: torch.Tensor, mask: Optional[torch.Tensor]) -> torch.Tensor:
+        plan = self.plan
+        assert plan is not None and self.final_ln is not None
+        batch, seq, d = x.shape
+        tokens = batch * seq
+        heads, hd = self.num_heads, self.head_dim
+
+        mask_u8 = lengths = flags = None
+        if mask is not None:
+            mask_u8 = mask.contiguous().view(torch.uint8) if mask.dtype == torch.bool \
+                else (mask != 0).to(torch.uint8)
+            lengths, flags = K.mask_lengths(mask_u8)
+
+        res = x.reshape(tokens, d)
+        if res.dtype != torch.float32 or not res.is_contiguous():
+            res = res.float().contiguous()
+        own_res = res.data_ptr() != x.data_ptr()
+        pending: Optional[torch.Tensor] = None
+        for lw in self.layers:
+            res, h = K.fused_add_layernorm(
+                res, pending, lw.ln1_w, lw.ln1_b, lw.ln1_eps, out_dtype=plan.compute_dtype,
+                residual_out=res if (own_res and pending is not None) else None)
+            own_res = own_res or pending is not None
+            qkv = K.gemm_bias(h, lw.wqkv, lw.bqkv)
+            ctx = K.flash_attention(qkv.view(batch, seq, 3, heads, hd), heads,
+                                    causal=self.causal, lengths=lengths, key_mask=mask_u8,
+                                    mask_flags=flags, scale=self.scale)
+            attn_out = K.gemm_bias(ctx, lw.wo, lw.bo, out_dtype=plan.delta_dtype)
+            res, h2 = K.fused_add_layernorm(
+                res, attn_out, lw.ln2_w, lw.ln2_b, lw.ln2_eps, out_dtype=plan.compute_dtype,
+                residual_out=res if own_res else None)
+            own_res = True
+            pending = K.fused_ffn(h2, lw.w1, lw.b1, lw.w2, lw.b2, out_dtype=plan.delta_dtype)
+
+        fw, fb, feps = self.final_ln
+        _, out = K.fused_add_layernorm(res, pending, fw, fb, feps, out_dtype=self.dtype,
+                                       write_residual=False, row_mask=mask_u8)
+        return out.view(batch, seq, d)
+
+    # ------------------------------------------------------------------- call
+
+    def __call__(self, x: torch.Tensor, mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if not x.is_cuda:
+            raise RuntimeError("tjkernels runs on CUDA (sm_100) tensors only; no CPU fallback")
+        batch, seq, _ = x.shape
+        plan = self._plan_cache.get((batch, seq))
+        if plan is None:
+            plan = select_plan(batch, seq, self.d_model, self.num_heads, self.ffn_dim,
+                               self.num_layers, self.causal, self.dtype, self.device)
+            self._plan_cache[(batch, seq)] = plan
+        self.plan = plan
+        self._build(plan)
+        if plan.cuda_graph:
+            key = (tuple(x.shape), x.dtype, mask is not None, plan)
+            return self._graphs.get(key, self._forward_impl, x, mask).run(x, mask)
+        return self._forward_impl(x, mask)
+
+
+def get_engine(module: torch.nn.Module) -> Engine:
+    engine = getattr(module, "_tj_engine", None)
+    param = next(module.parameters())
+    if engine is None or engine.dtype != param.dtype or engine.device != param.device:
+        engine = Engine(module)
+        object.__setattr__(module, "_tj_engine", engine)
+    return engine
+
+
+def reset_engines(module: torch.nn.Module) -> None:
+    if hasattr(module, "_tj_engine"):
+        object.__delattr__(module, "_tj_engine")
+
+
+def forward(module: torch.nn.Module, x: torch.Tensor,
+            valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The ``UserOptimizedTransformer.forward`` hook body."""
+    if os.environ.get("TJ_DISABLE") == "1":
+        return super(type(module), module).forward(x, valid_token_mask)
+    return get_engine(module)(x, valid_token_mask)

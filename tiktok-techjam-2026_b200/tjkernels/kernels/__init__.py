@@ -1,0 +1,185 @@
+"""Kernel facade: torch tensors in, torch tensors out, sm_100a kernels inside.
+
+Same functions and argument meaning as the reference facade
+(``tjkernels/kernels/__init__.py`` in the reference project):
+``fused_add_layernorm`` (:48-70), ``layernorm``, ``fused_ffn`` (:80-89) and
+``flash_attention`` (``tjkernels/kernels/attention.py:189-226``), plus
+``gemm_bias`` (the ``torch.addmm`` calls of ``engine.py:245,247``) and
+``mask_lengths`` (the device-side replacement of ``Engine._mask_mode``).
+
+Differences by design: there is no Triton and no torch fallback.  Every call
+runs the CUDA library on the tensor's device and current stream; a CPU tensor,
+an unsupported shape or dtype raises instead of silently switching backend.
+Outputs are allocated here with ``torch.empty`` (the caching allocator, so the
+calls capture into CUDA graphs); the library itself never allocates.
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from .. import _lib
+
+_CODES = {torch.float32: _lib.TJB_F32, torch.float16: _lib.TJB_F16,
+          torch.bfloat16: _lib.TJB_BF16}
+
+ACT_NONE, ACT_GELU = 0, 1
+
+
+def _code(dtype: torch.dtype) -> int:
+    try:
+        return _CODES[dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dtype}") from None
+
+
+def _need_cuda(*tensors: Optional[torch.Tensor]) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("tjkernels runs on CUDA (sm_100) tensors only; no CPU fallback")
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def fused_add_layernorm(
+    residual: torch.Tensor,
+    delta: Optional[torch.Tensor],
+    weight: torch.Tensor,
+    bias: torch.Tensor,
+    eps: float,
+    out_dtype: Optional[torch.dtype] = None,
+    write_residual: bool = True,
+    row_mask: Optional[torch.Tensor] = None,
+    residual_out: Optional[torch.Tensor] = None,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """``x = residual + delta``; return ``(x, layernorm(x))``.
+
+    ``residual`` is fp32 ``[rows, d]``; ``delta`` fp32/fp16/bf16 or None.
+    With ``write_residual=False`` the sum is not stored and the first result
+    is ``residual`` itself.  ``residual_out`` (may alias ``residual``) receives
+    the sum instead of a fresh tensor.  Rows with ``row_mask == 0`` (uint8)
+    get an exactly-zero normalised output.
+    """
+    _need_cuda(residual, delta, weight, bias, row_mask)
+    if residual.dtype != torch.float32:
+        raise TypeError("the residual stream is fp32")
+    rows, d = residual.shape
+    out_dtype = out_dtype or residual.dtype
+    out = torch.empty((rows, d), dtype=out_dtype, device=residual.device)
+    res_out = None
+    if write_residual and delta is not None:
+        res_out = residual_out if residual_out is not None else torch.empty_like(residual)
+    if delta is not None and not delta.is_contiguous():
+        delta = delta.contiguous()
+    status = _lib.lib().tjb_add_layernorm(
+        _ptr(residual), _ptr(delta), _ptr(res_out), _ptr(out), _ptr(weight), _ptr(bias),
+        rows, d, float(eps), _code(delta.dtype) if delta is not None else _lib.TJB_F32,
+        _code(out_dtype), _ptr(row_mask), _stream(residual.device))
+    _lib.check(status, "tjb_add_layernorm")
+    return (res_out if res_out is not None else residual), out
+
+
+def layernorm(x, weight, bias, eps, out_dtype=None):
+    """Plain LayerNorm over the last dim, emitting ``out_dtype`` directly."""
+    return fused_add_layernorm(x, None, weight, bias, eps, out_dtype=out_dtype,
+                               write_residual=False)[1]
+
+
+def gemm_bias(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],
+              act: int = ACT_NONE, out_dtype: Optional[torch.dtype] = None,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``act(a @ w.T + bias)``: a ``[M, K]``, w ``[N, K]`` (nn.Linear layout),
+    both fp16 or both bf16; bias fp32 ``[N]``; fp32 accumulation."""
+    _need_cuda(a, w, bias)
+    m, k = a.shape
+    n, k2 = w.shape
+    if k != k2:
+        raise ValueError(f"inner dims differ: {k} vs {k2}")
+    if a.dtype != w.dtype:
+        raise TypeError("a and w must share a dtype")
+    out_dtype = out_dtype or a.dtype
+    if out is None:
+        out = torch.empty((m, n), dtype=out_dtype, device=a.device)
+    status = _lib.lib().tjb_gemm_bias(
+        _ptr(a), _ptr(w), _ptr(bias), _ptr(out), m, n, k, a.stride(0), w.stride(0),
+        out.stride(0), _code(a.dtype), _code(out.dtype), act, _stream(a.device))
+    _lib.check(status, "tjb_gemm_bias")
+    return out
+
+
+def fused_ffn(h: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor, w2: torch.Tensor,
+              b2: torch.Tensor, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """``gelu_erf(h @ w1.T + b1) @ w2.T + b2``; w1 ``[F, d]``, w2 ``[d, F]``."""
+    _need_cuda(h, w1, b1, w2, b2)
+    t, d = h.shape
+    f = w1.shape[0]
+    out_dtype = out_dtype or h.dtype
+    out = torch.empty((t, d), dtype=out_dtype, device=h.device)
+    hidden = torch.empty((t, f), dtype=h.dtype, device=h.device)
+    status = _lib.lib().tjb_ffn(
+        _ptr(h), _ptr(w1), _ptr(b1), _ptr(w2), _ptr(b2), _ptr(out), _ptr(hidden), t, d, f,
+        _code(h.dtype), _code(out_dtype), _stream(h.device))
+    _lib.check(status, "tjb_ffn")
+    return out
+
+
+def flash_supports(head_dim: int, causal: bool = True) -> bool:
+    return head_dim in (64, 128)
+
+
+def flash_attention(qkv: torch.Tensor, heads: int, causal: bool = True,
+                    lengths: Optional[torch.Tensor] = None,
+                    key_mask: Optional[torch.Tensor] = None,
+                    mask_flags: Optional[torch.Tensor] = None,
+                    scale: Optional[float] = None) -> torch.Tensor:
+    """qkv ``[B, S, 3, H, hd]`` (contiguous) -> out ``[B*S, H*hd]``."""
+    _need_cuda(qkv, lengths, key_mask, mask_flags)
+    b, s, three, h, hd = qkv.shape
+    if three != 3 or h != heads:
+        raise ValueError("qkv must be [B, S, 3, H, hd]")
+    if not qkv.is_contiguous():
+        raise ValueError("qkv must be contiguous")
+    out = torch.empty((b * s, h * hd), dtype=qkv.dtype, device=qkv.device)
+    scale = hd ** -0.5 if scale is None else scale
+    status = _lib.lib().tjb_flash_fwd(
+        _ptr(qkv), _ptr(out), b, s, h, hd, float(scale), int(causal), _ptr(lengths),
+        _ptr(key_mask), _ptr(mask_flags), _code(qkv.dtype), _stream(qkv.device))
+    _lib.check(status, "tjb_flash_fwd")
+    return out
+
+
+def mask_lengths(mask: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Device-side padding-mask classification, no host sync.
+
+    Returns ``(lengths int32 [B], flags int32 [1])``; ``flags`` is 0 for a
+    prefix mask and non-zero otherwise.
+    """
+    _need_cuda(mask)
+    if mask.dtype == torch.bool:
+        mask = mask.contiguous().view(torch.uint8)
+    b, s = mask.shape
+    lengths = torch.empty((b,), dtype=torch.int32, device=mask.device)
+    flags = torch.empty((1,), dtype=torch.int32, device=mask.device)
+    status = _lib.lib().tjb_mask_lengths(_ptr(mask), b, s, _ptr(lengths), _ptr(flags),
+                                         _stream(mask.device))
+    _lib.check(status, "tjb_mask_lengths")
+    return lengths, flags
+
+
+def device_status(clear: bool = False) -> int:
+    """The device status word (0, or TJB_ERR_DEVICE_TIMEOUT); synchronises."""
+    return int(_lib.lib().tjb_device_status(int(clear)))
+
+
+__all__ = [
+    "ACT_NONE", "ACT_GELU", "fused_add_layernorm", "layernorm", "gemm_bias", "fused_ffn",
+    "flash_attention", "flash_supports", "mask_lengths", "device_status",
+]

@@ -1,0 +1,133 @@
+"""Shape -> execution-plan dispatch.
+
+Same surface as the reference's ``tjkernels/plans.py``: a frozen ``Plan`` of
+knobs (:29-67), ``shape_key`` (:70-77), ``default_plan`` heuristics
+(:80-134), a JSON table of tuned plans keyed by shape (:147-157),
+``set_override`` (:141-144), ``select_plan`` with ``TJ_*`` environment
+overrides (:160-190) and ``save_plans`` (:193-198).
+
+The knobs differ because there is one backend: the kernel-choice knobs of the
+reference (attn/ffn/norm = triton|torch|sdpa) are gone, and the remaining ones
+choose the tensor-core input type, the precision of the residual deltas and
+whether the whole forward is replayed as a CUDA graph.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+from dataclasses import dataclass, replace
+from pathlib import Path
+from typing import Dict, Optional
+
+import torch
+
+_PLAN_FILE = Path(__file__).with_name("plans.json")
+
+_DTYPES = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}
+_DTYPE_NAMES = {v: k for k, v in _DTYPES.items()}
+
+# A whole-forward graph costs one copy-in and one clone-out of the activations;
+# above this input size that copy is no longer free (reference: plans.py:107-110).
+GRAPH_MAX_INPUT_BYTES = 64 * 1024 * 1024
+
+
+@dataclass(frozen=True)
+class Plan:
+    """Execution knobs for one (shape, dtype) combination."""
+
+    # Tensor-core input type of every GEMM and of attention (fp32 accumulate).
+    compute_dtype: torch.dtype = torch.bfloat16
+    # Precision the residual stream is kept in (always fp32 here).
+    residual_dtype: torch.dtype = torch.float32
+    # Precision of the attention-output and FFN-output deltas that the next
+    # add+LayerNorm folds into the residual.
+    delta_dtype: torch.dtype = torch.float32
+    # Whole-forward CUDA graph replay.
+    cuda_graph: bool = True
+    label: str = "default"
+
+    def to_json(self) -> Dict[str, object]:
+        return {
+            "compute_dtype": _DTYPE_NAMES[self.compute_dtype],
+            "residual_dtype": _DTYPE_NAMES[self.residual_dtype],
+            "delta_dtype": _DTYPE_NAMES[self.delta_dtype],
+            "cuda_graph": self.cuda_graph,
+            "label": self.label,
+        }
+
+    @staticmethod
+    def from_json(blob: Dict[str, object]) -> "Plan":
+        blob = dict(blob)
+        for key, default in (("compute_dtype", "bfloat16"), ("residual_dtype", "float32"),
+                             ("delta_dtype", "float32")):
+            blob[key] = _DTYPES[str(blob.get(key, default))]
+        fields = Plan.__dataclass_fields__.keys()
+        return Plan(**{k: v for k, v in blob.items() if k in fields})
+
+
+def shape_key(batch: int, seq: int, d_model: int, heads: int, ffn_dim: int, layers: int,
+              causal: bool, dtype: torch.dtype) -> str:
+    return (f"b{batch}_s{seq}_d{d_model}_h{heads}_f{ffn_dim}_l{layers}"
+            f"_{'causal' if causal else 'full'}_{_DTYPE_NAMES[dtype]}")
+
+
+def default_plan(batch: int, seq: int, d_model: int, heads: int, ffn_dim: int, layers: int,
+                 causal: bool, dtype: torch.dtype, device: torch.device) -> Plan:
+    """Heuristic plan used when no tuned plan exists for the shape."""
+    if device.type != "cuda":
+        raise RuntimeError("tjkernels runs on CUDA (sm_100) devices only; no CPU fallback")
+    compute = dtype if dtype in (torch.float16, torch.bfloat16) else torch.bfloat16
+    x_bytes = batch * seq * d_model * torch.empty((), dtype=dtype).element_size()
+    return Plan(
+        compute_dtype=compute,
+        residual_dtype=torch.float32,
+        delta_dtype=torch.float32,
+        cuda_graph=x_bytes <= GRAPH_MAX_INPUT_BYTES,
+        label="heuristic",
+    )
+
+
+_cache: Optional[Dict[str, Plan]] = None
+_override: Optional[Plan] = None
+
+
+def set_override(plan: Optional[Plan]) -> None:
+    """Force one plan regardless of shape (tests, tuning)."""
+    global _override
+    _override = plan
+
+
+def _load_tuned() -> Dict[str, Plan]:
+    global _cache
+    if _cache is None:
+        _cache = {}
+        if _PLAN_FILE.exists() and os.environ.get("TJ_IGNORE_PLANS") != "1":
+            raw = json.loads(_PLAN_FILE.read_text())
+            _cache = {k: Plan.from_json(v) for k, v in raw.items()}
+    return _cache
+
+
+def select_plan(batch: int, seq: int, d_model: int, heads: int, ffn_dim: int, layers: int,
+                causal: bool, dtype: torch.dtype, device: torch.device) -> Plan:
+    if _override is not None:
+        return _override
+    key = shape_key(batch, seq, d_model, heads, ffn_dim, layers, causal, dtype)
+    plan = _load_tuned().get(key)
+    if plan is None:
+        plan = default_plan(batch, seq, d_model, heads, ffn_dim, layers, causal, dtype, device)
+    if os.environ.get("TJ_NO_GRAPH") == "1":
+        plan = replace(plan, cuda_graph=False)
+    forced = os.environ.get("TJ_COMPUTE_DTYPE")
+    if forced in ("float16", "bfloat16"):
+        plan = replace(plan, compute_dtype=_DTYPES[forced])
+    forced = os.environ.get("TJ_DELTA_DTYPE")
+    if forced in _DTYPES:
+        plan = replace(plan, delta_dtype=_DTYPES[forced])
+    return plan
+
+
+def save_plans(plans: Dict[str, Plan], path: Path = _PLAN_FILE) -> None:
+    path.write_text(json.dumps({k: v.to_json() for k, v in plans.items()}, indent=2) + "\n")
+    global _cache
+    _cache = None
