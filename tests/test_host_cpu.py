@@ -75,13 +75,13 @@ def test_plan_roundtrip_and_env(tmp_path, monkeypatch):
     monkeypatch.setenv("TJ_IGNORE_PLANS", "1")
     plans._cache = None
     base = plans.select_plan(2, 128, 512, 8, 2048, 4, True, torch.float32, dev)
-    assert base.compute_dtype == torch.bfloat16 and base.cuda_graph
+    assert base.compute_dtype == torch.float16 and base.cuda_graph
     big = plans.select_plan(64, 2048, 4096, 32, 16384, 12, True, torch.float32, dev)
     assert not big.cuda_graph  # 2 GB input: graph copy-in/clone-out not free
     monkeypatch.setenv("TJ_NO_GRAPH", "1")
-    monkeypatch.setenv("TJ_COMPUTE_DTYPE", "float16")
+    monkeypatch.setenv("TJ_COMPUTE_DTYPE", "bfloat16")
     forced = plans.select_plan(2, 128, 512, 8, 2048, 4, True, torch.float32, dev)
-    assert not forced.cuda_graph and forced.compute_dtype == torch.float16
+    assert not forced.cuda_graph and forced.compute_dtype == torch.bfloat16
     plans.set_override(p)
     try:
         assert plans.select_plan(1, 1, 1, 1, 1, 1, True, torch.float32, dev) is p
@@ -118,3 +118,18 @@ def test_tj_disable_runs_baseline(monkeypatch):
         out = model(x, m)
         ref = ReferenceModel.forward(model, x, m)
     assert torch.equal(out, ref)
+
+
+def test_oracle_ignores_subclass_forward():
+    """oracle_forward must run the reference math even on a hooked subclass."""
+    from oracle.model import ModelConfig, ReferenceModel, generate_case, oracle_forward
+
+    class Hooked(ReferenceModel):
+        def forward(self, x, valid_token_mask=None):
+            return torch.zeros_like(x)
+
+    cfg = ModelConfig(1, 8, 128, 2, 128, 1, True)
+    torch.manual_seed(0)
+    model = Hooked(cfg).eval()
+    x, m = generate_case(cfg, 0, 0.0)
+    assert oracle_forward(model, x, m).abs().sum() > 0

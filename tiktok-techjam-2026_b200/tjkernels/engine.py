@@ -35,6 +35,7 @@ from typing import Dict, List, Optional, Tuple
 import torch
 
 from .graphs import GraphCache
+from . import plans
 from .plans import Plan, select_plan
 from . import kernels as K
 
@@ -167,11 +168,12 @@ class Engine:
         if not x.is_cuda:
             raise RuntimeError("tjkernels runs on CUDA (sm_100) tensors only; no CPU fallback")
         batch, seq, _ = x.shape
-        plan = self._plan_cache.get((batch, seq))
+        plan = None if plans.has_override() else self._plan_cache.get((batch, seq))
         if plan is None:
             plan = select_plan(batch, seq, self.d_model, self.num_heads, self.ffn_dim,
                                self.num_layers, self.causal, self.dtype, self.device)
-            self._plan_cache[(batch, seq)] = plan
+            if not plans.has_override():
+                self._plan_cache[(batch, seq)] = plan
         self.plan = plan
         self._build(plan)
         if plan.cuda_graph:

@@ -1,0 +1,39 @@
+"""Batch sharding across GPUs (one process per GPU).
+
+Every layer of the encoder works within one sequence (row-wise GEMMs and
+LayerNorms, causal self-attention inside a sequence), so sequences are
+independent: a batch splits across ranks with no collective in the forward.
+Weights are replicated.  ``shard_range`` gives each rank a contiguous slice of
+the batch; ``balanced_shards`` instead balances the valid-token work when
+padded tiles are skipped.
+"""
+
+from __future__ import annotations
+
+from typing import List, Sequence, Tuple
+
+
+def shard_range(batch: int, world: int, rank: int) -> Tuple[int, int]:
+    """Contiguous [start, end) of sequences for ``rank``; sizes differ by <= 1."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of {world}")
+    base, extra = divmod(batch, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def balanced_shards(lengths: Sequence[int], world: int) -> List[List[int]]:
+    """Assign sequences to ranks so each rank's sum of causal work
+    (len*(len+1)/2 attention plus len for the GEMMs) is balanced: greedy
+    longest-first onto the least-loaded rank."""
+    if world <= 0:
+        raise ValueError("world must be positive")
+    order = sorted(range(len(lengths)), key=lambda i: -int(lengths[i]))
+    loads = [0.0] * world
+    shards: List[List[int]] = [[] for _ in range(world)]
+    for i in order:
+        n = int(lengths[i])
+        r = min(range(world), key=lambda k: (loads[k], k))
+        shards[r].append(i)
+        loads[r] += n * (n + 1) / 2 + n
+    return [sorted(s) for s in shards]

@@ -37,7 +37,7 @@ class Plan:
     """Execution knobs for one (shape, dtype) combination."""
 
     # Tensor-core input type of every GEMM and of attention (fp32 accumulate).
-    compute_dtype: torch.dtype = torch.bfloat16
+    compute_dtype: torch.dtype = torch.float16
     # Precision the residual stream is kept in (always fp32 here).
     residual_dtype: torch.dtype = torch.float32
     # Precision of the attention-output and FFN-output deltas that the next
@@ -59,7 +59,7 @@ class Plan:
     @staticmethod
     def from_json(blob: Dict[str, object]) -> "Plan":
         blob = dict(blob)
-        for key, default in (("compute_dtype", "bfloat16"), ("residual_dtype", "float32"),
+        for key, default in (("compute_dtype", "float16"), ("residual_dtype", "float32"),
                              ("delta_dtype", "float32")):
             blob[key] = _DTYPES[str(blob.get(key, default))]
         fields = Plan.__dataclass_fields__.keys()
@@ -77,7 +77,11 @@ def default_plan(batch: int, seq: int, d_model: int, heads: int, ffn_dim: int, l
     """Heuristic plan used when no tuned plan exists for the shape."""
     if device.type != "cuda":
         raise RuntimeError("tjkernels runs on CUDA (sm_100) devices only; no CPU fallback")
-    compute = dtype if dtype in (torch.float16, torch.bfloat16) else torch.bfloat16
+    # fp16 and bf16 run at the same tensor-core rate on sm_100; fp16 keeps 3
+    # more mantissa bits, which the per-element budget needs at d_model 4096 /
+    # 12 layers (bf16 measured 1.2x over budget there).  LayerNorm bounds
+    # every activation, so the fp16 range is never approached.
+    compute = dtype if dtype in (torch.float16, torch.bfloat16) else torch.float16
     x_bytes = batch * seq * d_model * torch.empty((), dtype=dtype).element_size()
     return Plan(
         compute_dtype=compute,
@@ -96,6 +100,10 @@ def set_override(plan: Optional[Plan]) -> None:
     """Force one plan regardless of shape (tests, tuning)."""
     global _override
     _override = plan
+
+
+def has_override() -> bool:
+    return _override is not None
 
 
 def _load_tuned() -> Dict[str, Plan]:
