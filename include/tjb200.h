@@ -126,6 +126,23 @@ int tjb_ffn(const void* h, const void* w1, const float* b1, const void* w2,
             int in_dtype, int out_dtype, tjb_stream_t stream);
 
 /*
+ * tjb_ffn without any device allocation and without caller scratch: the
+ * [T, F] hidden activations live in a 16 MiB device array inside the library
+ * (T * F <= TJB_FFN_NOALLOC_MAX_HIDDEN, else TJB_ERR_BAD_SHAPE and nothing is
+ * launched).  For callers that cannot allocate device memory when they run
+ * (a fixed memory pool with no allocator hook, or a path where an allocation
+ * may not block or fail).  Every GPU that loads the library holds the array
+ * until exit.  The first call on a device looks up the array's device
+ * address; make it before any stream capture.  All calls share the array:
+ * calls that overlap on the GPU race and must be serialised by the caller.
+ * No counterpart in the reference.
+ */
+#define TJB_FFN_NOALLOC_MAX_HIDDEN (8ll << 20)
+int tjb_ffn_noalloc(const void* h, const void* w1, const float* b1, const void* w2,
+                    const float* b2, void* out, int T, int d, int F,
+                    int in_dtype, int out_dtype, tjb_stream_t stream);
+
+/*
  * Classify a padding mask on the device, with no host synchronisation.
  * mask: uint8/bool [B, S].  lengths[b] = number of valid positions in row b.
  * *flags = 0 when every row is a prefix (positions < lengths[b]) and
