@@ -154,6 +154,12 @@ int tjb_mask_lengths(const uint8_t* mask, int B, int S, int32_t* lengths,
                      int32_t* flags, tjb_stream_t stream);
 
 /*
+ * Text of the last CUDA error this library saw on the calling thread (the
+ * cause behind a TJB_ERR_LAUNCH).  No counterpart in the reference.
+ */
+const char* tjb_last_cuda_error(void);
+
+/*
  * Device status word of the current device: TJB_OK, or the first error a
  * kernel recorded (TJB_ERR_DEVICE_TIMEOUT).  Synchronises the device.  When
  * clear != 0 the word is reset to TJB_OK afterwards.

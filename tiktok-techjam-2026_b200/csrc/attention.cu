@@ -381,6 +381,424 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ===========================================================================
+// Paired-tile persistent kernel (head_dim 64).
+//
+// Each CTA (one per SM) walks work items (batch*head, pair of consecutive
+// 128-row query tiles), heaviest causal rows first.  The two query tiles are
+// owned by two softmax warp groups that run in lock-step against one MMA
+// issuer, so while group 0 computes its softmax the tensor core works on
+// group 1's products and vice versa; K/V tiles are loaded once for both.
+//   warp 0        TMA producer (Q pair once per item, then K/V tiles)
+//   warp 1        TMEM owner + MMA issuer:
+//                   S_g = Q_g K_j^T  (g = 0, 1), as soon as group g has
+//                   pulled its previous scores out of TMEM;
+//                   O_g += P_g V_j   once group g has written P_g.
+//   warps 2-5     softmax group 0 (query rows q0 .. q0+127)
+//   warps 6-9     softmax group 1 (query rows q0+128 .. q0+255)
+// Ten warps put three on two of the SM's four sub-partitions, which caps a
+// thread at 168 registers; the softmax (a 128-score row in registers) fits.
+// P is double-buffered in shared memory per group.  O is rescaled lazily:
+// only when a row's max grows by more than 2^8 (so P stays below 256 in
+// 16-bit and every sum stays in fp32 range); the final O / l is exact for
+// any choice of the reference max.
+constexpr int kPairThreads = 320;
+
+constexpr float kRescaleLog2 = 8.0f;
+
+struct PairCfg {
+  static constexpr int HD = 64;
+  static constexpr int kStages = 2;
+  static constexpr uint32_t kQBytes = kSub;       // one 128 x 64 tile per group
+  static constexpr uint32_t kKVBytes = 2 * kSub;  // K tile + V tile
+  static constexpr uint32_t kPBytes = 2 * kSub;   // 128 x 128
+  static constexpr uint32_t kSmemBytes =
+      1024 + 2 * kQBytes + kStages * kKVBytes + 4 * kPBytes + 256;
+  static constexpr uint32_t kTmemCols = 512;  // S0 0, S1 128, O0 256, O1 320
+  static constexpr uint32_t kOCol = 256;
+};
+
+struct PairItem {
+  int b, h, q0;
+  int n_kv[2];
+  int kv_len;
+};
+
+__device__ __forceinline__ PairItem decode_pair(int w, const AttnArgs& a, int num_pairs,
+                                                bool prefix) {
+  PairItem it;
+  const int bh_count = a.B * a.H;
+  const int pr = num_pairs - 1 - w / bh_count;
+  const int bh = w - (w / bh_count) * bh_count;
+  it.b = bh / a.H;
+  it.h = bh - it.b * a.H;
+  it.q0 = pr * 2 * kTileQ;
+  int kv_len = a.S;
+  if (prefix) kv_len = min(max(__ldg(a.lengths + it.b), 0), a.S);
+  it.kv_len = kv_len;
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {
+    const int qs = it.q0 + g * kTileQ;
+    int n = 0;
+    if (qs < kv_len || (!prefix && qs < a.S)) {
+      n = (kv_len + kTileK - 1) / kTileK;
+      if (a.causal) n = min(n, qs / kTileK + 1);
+    }
+    it.n_kv[g] = n;
+  }
+  return it;
+}
+
+__global__ void __launch_bounds__(kPairThreads, 1)
+    attn_pair_kernel(const __grid_constant__ CUtensorMap tm, const AttnArgs args) {
+  using Cfg = PairCfg;
+  constexpr int HD = Cfg::HD;
+  constexpr int kStages = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem;                                 // [2][kQBytes]
+  uint8_t* sKV = sQ + 2 * Cfg::kQBytes;               // [kStages][K | V]
+  uint8_t* sP = sKV + kStages * Cfg::kKVBytes;        // [group][buf][kPBytes]
+  uint64_t* q_full = reinterpret_cast<uint64_t*>(sP + 4 * Cfg::kPBytes);
+  uint64_t* q_empty = q_full + 1;
+  uint64_t* kv_full = q_empty + 1;
+  uint64_t* kv_empty = kv_full + kStages;
+  uint64_t* s_full = kv_empty + kStages;  // [2]
+  uint64_t* s_free = s_full + 2;          // [2]
+  uint64_t* p_full = s_free + 2;          // [group*2 + buf]
+  uint64_t* pv_done = p_full + 4;         // [group*2 + buf]
+  uint64_t* drain = pv_done + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_pairs = (args.S + 2 * kTileQ - 1) / (2 * kTileQ);
+  const int total = args.B * args.H * num_pairs;
+  const bool prefix = args.lengths != nullptr &&
+                      (args.mask_flags == nullptr || __ldg(args.mask_flags) == 0);
+  const bool use_key_mask = args.key_mask != nullptr && !prefix;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(&s_full[g], 1);
+      mbar_init(&s_free[g], 4);
+    }
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&p_full[i], 4);
+      mbar_init(&pv_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tm);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // -------------------------------------------------------------- producer
+      int stage = 0;
+      uint32_t phase = 0, issued = 0, issued_parity = 0, q_count = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+        const PairItem it = decode_pair(w, args, num_pairs, prefix);
+        const int n = max(it.n_kv[0], it.n_kv[1]);
+        if (n == 0) continue;
+        if (q_count > 0 && !mbar_wait(q_empty, (q_count - 1) & 1, abort_flag)) break;
+        const int colQ = it.h * HD;
+        const int ntiles = (it.n_kv[0] > 0) + (it.n_kv[1] > 0);
+        mbar_arrive_expect_tx(q_full, ntiles * Cfg::kQBytes);
+        for (int g = 0; g < 2; ++g)
+          if (it.n_kv[g] > 0)
+            tma_load_3d(sQ + g * Cfg::kQBytes, &tm, q_full, colQ, it.q0 + g * kTileQ, it.b);
+        ++q_count;
+        const int colK = (args.H + it.h) * HD;
+        const int colV = (2 * args.H + it.h) * HD;
+        for (int j = 0; j < n; ++j) {
+          if (!mbar_wait(&kv_empty[stage], phase ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sK = sKV + stage * Cfg::kKVBytes;
+          mbar_arrive_expect_tx(&kv_full[stage], Cfg::kKVBytes);
+          tma_load_3d(sK, &tm, &kv_full[stage], colK, j * kTileK, it.b);
+          tma_load_3d(sK + kSub, &tm, &kv_full[stage], colV, j * kTileK, it.b);
+          issued |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (q_count > 0) mbar_wait_drain(q_full, (q_count - 1) & 1);
+      for (int s = 0; s < kStages; ++s)
+        if ((issued >> s) & 1u) mbar_wait_drain(&kv_full[s], (issued_parity >> s) & 1u);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      const uint32_t q_addr = smem_u32(sQ);
+      const uint32_t p_addr = smem_u32(sP);
+      int stage = 0, prev_stage = 0;
+      uint32_t phase = 0, q_count = 0;
+      uint32_t sc[2] = {0, 0}, pvc[2] = {0, 0};
+      bool ok = true;
+      for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+        const PairItem it = decode_pair(w, args, num_pairs, prefix);
+        const int n = max(it.n_kv[0], it.n_kv[1]);
+        if (n == 0) continue;
+        if (!mbar_wait(q_full, q_count & 1, abort_flag)) break;
+        ++q_count;
+        for (int j = 0; j <= n && ok; ++j) {
+          if (j < n) {
+            if (!mbar_wait(&kv_full[stage], phase, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t k_addr = smem_u32(sKV + stage * Cfg::kKVBytes);
+            for (int g = 0; g < 2 && ok; ++g) {
+              if (j >= it.n_kv[g]) continue;
+              if (sc[g] > 0 && !mbar_wait(&s_free[g], (sc[g] - 1) & 1, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t qa = q_addr + g * Cfg::kQBytes;
+              const uint32_t d_s = tmem_base + static_cast<uint32_t>(g * kTileK);
+#pragma unroll
+              for (int k = 0; k < HD / 16; ++k)
+                umma_ss(d_s, sdesc_sw128(qa + k * 32, 16, 1024),
+                        sdesc_sw128(k_addr + k * 32, 16, 1024), args.idesc_qk, k > 0 ? 1u : 0u);
+              umma_commit(&s_full[g]);
+              ++sc[g];
+            }
+            if (!ok) break;
+            if (j == n - 1) umma_commit(q_empty);
+          }
+          if (j >= 1) {
+            const int jp = j - 1;
+            const uint32_t v_addr = smem_u32(sKV + prev_stage * Cfg::kKVBytes) + kSub;
+            for (int g = 0; g < 2 && ok; ++g) {
+              if (jp >= it.n_kv[g]) continue;
+              const uint32_t t = pvc[g];
+              uint64_t* pf = &p_full[g * 2 + (t & 1)];
+              if (!mbar_wait(pf, (t >> 1) & 1, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t pa = p_addr + (g * 2 + (t & 1)) * Cfg::kPBytes;
+              const uint32_t d_o = tmem_base + Cfg::kOCol + g * HD;
+#pragma unroll
+              for (int k = 0; k < kTileK / 16; ++k) {
+                const uint32_t a_off = (k >> 2) * kSub + (k & 3) * 32;
+                umma_ss(d_o, sdesc_sw128(pa + a_off, 16, 1024),
+                        sdesc_sw128(v_addr + k * 2048, kSub, 1024), args.idesc_pv,
+                        (jp > 0 || k > 0) ? 1u : 0u);
+              }
+              umma_commit(&pv_done[g * 2 + (t & 1)]);
+              ++pvc[g];
+            }
+            if (!ok) break;
+            umma_commit(&kv_empty[prev_stage]);
+          }
+          if (j < n) {
+            prev_stage = stage;
+            if (++stage == kStages) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+        }
+      }
+      umma_commit(drain);
+      mbar_wait_drain(drain, 0);
+    }
+  } else if (warp >= 2) {
+    // -------------------------------------------------------------- softmax
+    const int g = (warp - 2) >> 2;  // group 0: warps 2-5, group 1: warps 6-9
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t s_col = static_cast<uint32_t>(g * kTileK);
+    const uint32_t o_col = Cfg::kOCol + g * HD;
+    const float sl2 = args.scale_log2;
+    uint32_t t = 0;  // tiles this group has processed (all items)
+    bool ok = true;
+    for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+      const PairItem it = decode_pair(w, args, num_pairs, prefix);
+      const int qs = it.q0 + g * kTileQ;
+      const int qi = qs + r;
+      uint16_t* out_ptr = static_cast<uint16_t*>(args.out) +
+                          (static_cast<int64_t>(it.b) * args.S + qi) * args.ldo + it.h * HD;
+      const int nk = it.n_kv[g];
+      if (nk == 0) {
+        if (qi < args.S) {
+#pragma unroll
+          for (int c = 0; c < HD / 8; ++c)
+            reinterpret_cast<uint4*>(out_ptr)[c] = make_uint4(0u, 0u, 0u, 0u);
+        }
+        continue;
+      }
+      const uint8_t* km =
+          use_key_mask ? args.key_mask + static_cast<int64_t>(it.b) * args.S : nullptr;
+      float m_ref = -INFINITY;  // reference max the exponentials are taken against
+      float l_i = 0.f;
+      for (int j = 0; j < nk; ++j) {
+        bool w_ok = mbar_wait(&s_full[g], t & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, w_ok)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t sv[kTileK];
+#pragma unroll
+        for (int c = 0; c < kTileK / 32; ++c) tmem_ld32p(lane_base + s_col + c * 32, sv + c * 32);
+        tmem_ld_wait_n<kTileK>(sv);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[g]);  // scores are in registers now
+        const int kv0 = j * kTileK;
+        const bool need_mask = (args.causal && kv0 + kTileK - 1 > qs) ||
+                               (kv0 + kTileK > it.kv_len) || use_key_mask;
+        if (need_mask) {
+#pragma unroll
+          for (int c = 0; c < kTileK; ++c) {
+            const int kj = kv0 + c;
+            bool masked = kj >= it.kv_len || (args.causal && kj > qi);
+            if (km != nullptr && kj < args.S && km[kj] == 0) masked = true;
+            if (masked) sv[c] = __float_as_uint(-INFINITY);
+          }
+        }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < kTileK; ++c) mx = fmaxf(mx, __uint_as_float(sv[c]));
+        const float m_new = fmaxf(m_ref, mx);
+        const bool grow = m_new > m_ref && (m_ref == -INFINITY || (m_new - m_ref) * sl2 > kRescaleLog2);
+        const float alpha = grow ? fast_exp2((m_ref - m_new) * sl2) : 1.f;
+        if (grow) {
+          l_i *= alpha;
+          m_ref = m_new;
+        }
+        const float mb = m_ref == -INFINITY ? 0.f : m_ref * sl2;
+        // P buffer (t & 1) is free once the PV of this group's tile t-2 is done.
+        if (t >= 2) {
+          const uint32_t tq = t - 2;
+          w_ok = mbar_wait(&pv_done[g * 2 + (tq & 1)], (tq >> 1) & 1, abort_flag);
+          if (!__all_sync(0xffffffffu, w_ok)) {
+            ok = false;
+            break;
+          }
+        }
+        uint8_t* prow = sP + (g * 2 + (t & 1)) * Cfg::kPBytes + r * 128;
+        float rowsum = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < kTileK / 8; ++cc) {
+          float e[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            e[i] = fast_exp2(fmaf(__uint_as_float(sv[cc * 8 + i]), sl2, -mb));
+            rowsum += e[i];
+          }
+          uint4 v;
+          if (args.bf16) {
+            v.x = Pack2<__nv_bfloat16>::pack(e[0], e[1]);
+            v.y = Pack2<__nv_bfloat16>::pack(e[2], e[3]);
+            v.z = Pack2<__nv_bfloat16>::pack(e[4], e[5]);
+            v.w = Pack2<__nv_bfloat16>::pack(e[6], e[7]);
+          } else {
+            v.x = Pack2<__half>::pack(e[0], e[1]);
+            v.y = Pack2<__half>::pack(e[2], e[3]);
+            v.z = Pack2<__half>::pack(e[4], e[5]);
+            v.w = Pack2<__half>::pack(e[6], e[7]);
+          }
+          const int sub = cc >> 3, c8 = cc & 7;
+          *reinterpret_cast<uint4*>(prow + sub * kSub + ((c8 ^ (r & 7)) << 4)) = v;
+        }
+        l_i += rowsum;
+        // Rescale O (after the previous PV has landed) before this tile's PV.
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {
+          const uint32_t tp = t - 1;
+          w_ok = mbar_wait(&pv_done[g * 2 + (tp & 1)], (tp >> 1) & 1, abort_flag);
+          if (!__all_sync(0xffffffffu, w_ok)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t o[32];
+            const uint32_t ta = lane_base + o_col + c * 32;
+            tmem_ld32(ta, o);
+            tmem_ld_wait(o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(ta, o);
+          }
+          tmem_st_wait();
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[g * 2 + (t & 1)]);
+        ++t;
+      }
+      if (!ok) break;
+      // Epilogue: O / l once the item's last PV has landed.
+      const uint32_t tl = t - 1;
+      const bool w_ok = mbar_wait(&pv_done[g * 2 + (tl & 1)], (tl >> 1) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, w_ok)) break;
+      tc_fence_after();
+      const float inv_l = l_i > 0.f ? 1.f / l_i : 0.f;
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(lane_base + o_col + c * 32, o);
+        tmem_ld_wait(o);
+        if (qi < args.S) {
+          uint32_t p[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float x0 = __uint_as_float(o[2 * i]) * inv_l;
+            const float x1 = __uint_as_float(o[2 * i + 1]) * inv_l;
+            p[i] = args.bf16 ? Pack2<__nv_bfloat16>::pack(x0, x1) : Pack2<__half>::pack(x0, x1);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(out_ptr + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            dst[i] = make_uint4(p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
+        }
+      }
+      tc_fence_before();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
 std::mutex g_attn_attr_mu;
 bool g_attn_attr_done[64][2];
 
@@ -393,9 +811,9 @@ int launch_attn(const void* qkv, const AttnArgs& args, cudaStream_t stream) {
     std::lock_guard<std::mutex> lock(g_attn_attr_mu);
     const int slot = HD == 64 ? 0 : 1;
     if (dev < 64 && !g_attn_attr_done[dev][slot]) {
-      if (cudaFuncSetAttribute(attn_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(Cfg::kSmemBytes)) != cudaSuccess)
-        return TJB_ERR_LAUNCH;
+      if (const int fs = cuda_status(cudaFuncSetAttribute(attn_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(Cfg::kSmemBytes))))
+        return fs;
       g_attn_attr_done[dev][slot] = true;
     }
   }
@@ -408,6 +826,34 @@ int launch_attn(const void* qkv, const AttnArgs& args, cudaStream_t stream) {
   if (st != TJB_OK) return st;
   dim3 grid(args.B * args.H, (args.S + kTileQ - 1) / kTileQ);
   attn_fwd_kernel<HD><<<grid, 192, Cfg::kSmemBytes, stream>>>(tm, args);
+  return launch_status();
+}
+
+std::mutex g_pair_attr_mu;
+bool g_pair_attr_done[64];
+
+int launch_attn_pair(const void* qkv, const AttnArgs& args, cudaStream_t stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(g_pair_attr_mu);
+    if (dev < 64 && !g_pair_attr_done[dev]) {
+      if (const int fs = cuda_status(cudaFuncSetAttribute(attn_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(PairCfg::kSmemBytes))))
+        return fs;
+      g_pair_attr_done[dev] = true;
+    }
+  }
+  CUtensorMap tm;
+  const uint64_t row = 3ull * args.H * PairCfg::HD;
+  const uint64_t dims[3] = {row, static_cast<uint64_t>(args.S), static_cast<uint64_t>(args.B)};
+  const uint64_t strides[2] = {row * 2, row * 2 * static_cast<uint64_t>(args.S)};
+  const uint32_t box[3] = {64, 128, 1};
+  const int st = make_tmap_16bit(&tm, 3, qkv, dims, strides, box, args.bf16 != 0);
+  if (st != TJB_OK) return st;
+  const long total = static_cast<long>(args.B) * args.H * ((args.S + 2 * kTileQ - 1) / (2 * kTileQ));
+  const int grid = static_cast<int>(total < num_sms() ? total : num_sms());
+  attn_pair_kernel<<<grid, kPairThreads, PairCfg::kSmemBytes, stream>>>(tm, args);
   return launch_status();
 }
 
@@ -439,5 +885,5 @@ extern "C" int tjb_flash_fwd(const void* qkv, void* out, int B, int S, int H, in
   a.idesc_qk = idesc_f16(kTileQ, kTileK, a.bf16 != 0, false);
   a.idesc_pv = idesc_f16(kTileQ, hd, a.bf16 != 0, true);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  return hd == 64 ? launch_attn<64>(qkv, a, s) : launch_attn<128>(qkv, a, s);
+  return hd == 64 ? launch_attn_pair(qkv, a, s) : launch_attn<128>(qkv, a, s);
 }

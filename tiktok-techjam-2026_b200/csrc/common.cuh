@@ -220,6 +220,21 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "memory");
 }
 
+// Same load into 32 consecutive elements of a larger register array.
+__device__ __forceinline__ void tmem_ld32p(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -240,6 +255,14 @@ __device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(r[i]));
+}
+
+// Wait for outstanding tcgen05.ld and pin N loaded registers after it.
+template <int N>
+__device__ __forceinline__ void tmem_ld_wait_n(uint32_t* r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
 }
 
 __device__ __forceinline__ void tmem_st_wait() {
@@ -284,10 +307,19 @@ bool device_ok();
 int make_tmap_16bit(CUtensorMap* map, int rank, const void* base, const uint64_t* dims,
                     const uint64_t* strides_bytes, const uint32_t* box, bool bf16);
 
-inline int launch_status() {
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? TJB_OK : TJB_ERR_LAUNCH;
+// Last CUDA error seen by this library on the calling thread.
+inline cudaError_t& last_cuda_error() {
+  static thread_local cudaError_t e = cudaSuccess;
+  return e;
 }
+
+inline int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return TJB_OK;
+  last_cuda_error() = e;
+  return TJB_ERR_LAUNCH;
+}
+
+inline int launch_status() { return cuda_status(cudaGetLastError()); }
 
 inline bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;

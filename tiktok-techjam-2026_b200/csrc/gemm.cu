@@ -280,9 +280,9 @@ int launch_gemm(const void* A, const void* B, const GemmArgs& args, int lda, int
   {
     std::lock_guard<std::mutex> lock(g_attr_mu);
     if (dev < 64 && !g_attr_done[dev][slot]) {
-      if (cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(Cfg::kSmemBytes)) != cudaSuccess)
-        return TJB_ERR_LAUNCH;
+      if (const int fs = cuda_status(cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(Cfg::kSmemBytes))))
+        return fs;
       g_attr_done[dev][slot] = true;
     }
   }

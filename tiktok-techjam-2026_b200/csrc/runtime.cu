@@ -162,6 +162,10 @@ const char* tjb_status_string(int status) {
   }
 }
 
+const char* tjb_last_cuda_error(void) {
+  return cudaGetErrorString(tjb::last_cuda_error());
+}
+
 int tjb_device_status(int clear) {
   if (cudaDeviceSynchronize() != cudaSuccess) return TJB_ERR_LAUNCH;
   int v = 0;

@@ -21,6 +21,7 @@ _c_int, _c_i64, _c_f32, _p = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctype
 SIGNATURES = {
     "tjb_version": (_c_int, []),
     "tjb_status_string": (ctypes.c_char_p, [_c_int]),
+    "tjb_last_cuda_error": (ctypes.c_char_p, []),
     "tjb_add_layernorm": (_c_int, [_p, _p, _p, _p, _p, _p, _c_i64, _c_int, _c_f32,
                                    _c_int, _c_int, _p, _p]),
     "tjb_gemm_bias": (_c_int, [_p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int,
@@ -74,4 +75,6 @@ def lib() -> ctypes.CDLL:
 def check(status: int, what: str) -> None:
     if status != 0:
         msg = lib().tjb_status_string(status).decode()
+        if status == 5:  # TJB_ERR_LAUNCH: add the CUDA error behind it
+            msg += ": " + lib().tjb_last_cuda_error().decode()
         raise KernelError(what, status, msg)
