@@ -386,10 +386,12 @@ __global__ void __launch_bounds__(192, 1)
 //
 // Each CTA (one per SM) walks work items (batch*head, pair of consecutive
 // 128-row query tiles), heaviest causal rows first.  The two query tiles are
-// owned by two softmax warp groups that run in lock-step against one MMA
-// issuer, so while group 0 computes its softmax the tensor core works on
-// group 1's products and vice versa; K/V tiles are loaded once for both.
-//   warp 0        TMA producer (Q pair once per item, then K/V tiles)
+// owned by two softmax warp groups that run against one MMA issuer, so while
+// group 0 computes its softmax the tensor core works on group 1's products
+// and vice versa; K/V tiles are loaded once for both groups.
+//   warp 0        TMA producer: the next item's Q pair (double-buffered, so
+//                 it lands while the current item runs), then K/V tiles into
+//                 a 4-stage ring
 //   warp 1        TMEM owner + MMA issuer:
 //                   S_g = Q_g K_j^T  (g = 0, 1), as soon as group g has
 //                   pulled its previous scores out of TMEM;
@@ -398,24 +400,27 @@ __global__ void __launch_bounds__(192, 1)
 //   warps 6-9     softmax group 1 (query rows q0+128 .. q0+255)
 // Ten warps put three on two of the SM's four sub-partitions, which caps a
 // thread at 168 registers; the softmax (a 128-score row in registers) fits.
-// P is double-buffered in shared memory per group.  O is rescaled lazily:
-// only when a row's max grows by more than 2^8 (so P stays below 256 in
-// 16-bit and every sum stays in fp32 range); the final O / l is exact for
-// any choice of the reference max.
+// P lives in tensor memory (one buffer per group; the PV MMA reads it as its
+// A operand), so it never round-trips through shared memory.  Each group's
+// exponentials are computed into registers before P is overwritten, so the
+// wait for the previous PV overlaps the math.
+// O is rescaled lazily: only when a row's max grows by more than 2^8 (P stays
+// below 256 in 16-bit, every sum stays in fp32 range); O / l is exact for any
+// choice of the reference max.
 constexpr int kPairThreads = 320;
-
 constexpr float kRescaleLog2 = 8.0f;
 
 struct PairCfg {
   static constexpr int HD = 64;
-  static constexpr int kStages = 2;
+  static constexpr int kStages = 4;
   static constexpr uint32_t kQBytes = kSub;       // one 128 x 64 tile per group
   static constexpr uint32_t kKVBytes = 2 * kSub;  // K tile + V tile
-  static constexpr uint32_t kPBytes = 2 * kSub;   // 128 x 128
-  static constexpr uint32_t kSmemBytes =
-      1024 + 2 * kQBytes + kStages * kKVBytes + 4 * kPBytes + 256;
-  static constexpr uint32_t kTmemCols = 512;  // S0 0, S1 128, O0 256, O1 320
+  static constexpr uint32_t kSmemBytes = 1024 + 4 * kQBytes + kStages * kKVBytes + 256;
+  // TMEM columns: S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384)
+  // P0 [384,448) P1 [448,512) (P: 128 x 128 16-bit, two values per column).
+  static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kOCol = 256;
+  static constexpr uint32_t kPCol = 384;
 };
 
 struct PairItem {
@@ -449,6 +454,7 @@ __device__ __forceinline__ PairItem decode_pair(int w, const AttnArgs& a, int nu
   return it;
 }
 
+template <bool kBF16>
 __global__ void __launch_bounds__(kPairThreads, 1)
     attn_pair_kernel(const __grid_constant__ CUtensorMap tm, const AttnArgs args) {
   using Cfg = PairCfg;
@@ -457,18 +463,17 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint8_t* sQ = smem;                                 // [2][kQBytes]
-  uint8_t* sKV = sQ + 2 * Cfg::kQBytes;               // [kStages][K | V]
-  uint8_t* sP = sKV + kStages * Cfg::kKVBytes;        // [group][buf][kPBytes]
-  uint64_t* q_full = reinterpret_cast<uint64_t*>(sP + 4 * Cfg::kPBytes);
-  uint64_t* q_empty = q_full + 1;
-  uint64_t* kv_full = q_empty + 1;
+  uint8_t* sQ = smem;                                 // [slot][group][kQBytes]
+  uint8_t* sKV = sQ + 4 * Cfg::kQBytes;               // [kStages][K | V]
+  uint64_t* q_full = reinterpret_cast<uint64_t*>(sKV + kStages * Cfg::kKVBytes);  // [slot]
+  uint64_t* q_empty = q_full + 2;                                          // [slot]
+  uint64_t* kv_full = q_empty + 2;
   uint64_t* kv_empty = kv_full + kStages;
-  uint64_t* s_full = kv_empty + kStages;  // [2]
-  uint64_t* s_free = s_full + 2;          // [2]
-  uint64_t* p_full = s_free + 2;          // [group*2 + buf]
-  uint64_t* pv_done = p_full + 4;         // [group*2 + buf]
-  uint64_t* drain = pv_done + 4;
+  uint64_t* s_full = kv_empty + kStages;  // [group]
+  uint64_t* s_free = s_full + 2;          // [group]
+  uint64_t* p_full = s_free + 2;          // [group]
+  uint64_t* pv_done = p_full + 2;         // [group]
+  uint64_t* drain = pv_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -481,19 +486,17 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   const bool use_key_mask = args.key_mask != nullptr && !prefix;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&pv_done[i], 1);
+    }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
-    }
-    for (int g = 0; g < 2; ++g) {
-      mbar_init(&s_full[g], 1);
-      mbar_init(&s_free[g], 4);
-    }
-    for (int i = 0; i < 4; ++i) {
-      mbar_init(&p_full[i], 4);
-      mbar_init(&pv_done[i], 1);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -513,20 +516,24 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     if (lane == 0) {
       // -------------------------------------------------------------- producer
       int stage = 0;
-      uint32_t phase = 0, issued = 0, issued_parity = 0, q_count = 0;
+      uint32_t phase = 0, issued = 0, issued_parity = 0, n_items = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
         const PairItem it = decode_pair(w, args, num_pairs, prefix);
         const int n = max(it.n_kv[0], it.n_kv[1]);
         if (n == 0) continue;
-        if (q_count > 0 && !mbar_wait(q_empty, (q_count - 1) & 1, abort_flag)) break;
+        const uint32_t slot = n_items & 1;
+        // The slot was last used by item n_items - 2.
+        if (n_items >= 2 && !mbar_wait(&q_empty[slot], ((n_items - 2) >> 1) & 1, abort_flag))
+          break;
         const int colQ = it.h * HD;
         const int ntiles = (it.n_kv[0] > 0) + (it.n_kv[1] > 0);
-        mbar_arrive_expect_tx(q_full, ntiles * Cfg::kQBytes);
+        mbar_arrive_expect_tx(&q_full[slot], ntiles * Cfg::kQBytes);
         for (int g = 0; g < 2; ++g)
           if (it.n_kv[g] > 0)
-            tma_load_3d(sQ + g * Cfg::kQBytes, &tm, q_full, colQ, it.q0 + g * kTileQ, it.b);
-        ++q_count;
+            tma_load_3d(sQ + (slot * 2 + g) * Cfg::kQBytes, &tm, &q_full[slot], colQ,
+                        it.q0 + g * kTileQ, it.b);
+        ++n_items;
         const int colK = (args.H + it.h) * HD;
         const int colV = (2 * args.H + it.h) * HD;
         for (int j = 0; j < n; ++j) {
@@ -546,25 +553,27 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           }
         }
       }
-      if (q_count > 0) mbar_wait_drain(q_full, (q_count - 1) & 1);
+      for (uint32_t k = n_items >= 2 ? n_items - 2 : 0; k < n_items; ++k)
+        mbar_wait_drain(&q_full[k & 1], (k >> 1) & 1);
       for (int s = 0; s < kStages; ++s)
         if ((issued >> s) & 1u) mbar_wait_drain(&kv_full[s], (issued_parity >> s) & 1u);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------------------ MMA issuer
-      const uint32_t q_addr = smem_u32(sQ);
-      const uint32_t p_addr = smem_u32(sP);
+      const uint32_t q_base = smem_u32(sQ);
       int stage = 0, prev_stage = 0;
-      uint32_t phase = 0, q_count = 0;
+      uint32_t phase = 0, n_items = 0;
       uint32_t sc[2] = {0, 0}, pvc[2] = {0, 0};
       bool ok = true;
       for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
         const PairItem it = decode_pair(w, args, num_pairs, prefix);
         const int n = max(it.n_kv[0], it.n_kv[1]);
         if (n == 0) continue;
-        if (!mbar_wait(q_full, q_count & 1, abort_flag)) break;
-        ++q_count;
+        const uint32_t slot = n_items & 1;
+        if (!mbar_wait(&q_full[slot], (n_items >> 1) & 1, abort_flag)) break;
+        ++n_items;
+        const uint32_t q_addr = q_base + slot * 2 * Cfg::kQBytes;
         for (int j = 0; j <= n && ok; ++j) {
           if (j < n) {
             if (!mbar_wait(&kv_full[stage], phase, abort_flag)) {
@@ -590,30 +599,25 @@ __global__ void __launch_bounds__(kPairThreads, 1)
               ++sc[g];
             }
             if (!ok) break;
-            if (j == n - 1) umma_commit(q_empty);
+            if (j == n - 1) umma_commit(&q_empty[slot]);
           }
           if (j >= 1) {
             const int jp = j - 1;
             const uint32_t v_addr = smem_u32(sKV + prev_stage * Cfg::kKVBytes) + kSub;
             for (int g = 0; g < 2 && ok; ++g) {
               if (jp >= it.n_kv[g]) continue;
-              const uint32_t t = pvc[g];
-              uint64_t* pf = &p_full[g * 2 + (t & 1)];
-              if (!mbar_wait(pf, (t >> 1) & 1, abort_flag)) {
+              if (!mbar_wait(&p_full[g], pvc[g] & 1, abort_flag)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
-              const uint32_t pa = p_addr + (g * 2 + (t & 1)) * Cfg::kPBytes;
+              const uint32_t pa = tmem_base + Cfg::kPCol + g * (kTileK / 2);
               const uint32_t d_o = tmem_base + Cfg::kOCol + g * HD;
 #pragma unroll
-              for (int k = 0; k < kTileK / 16; ++k) {
-                const uint32_t a_off = (k >> 2) * kSub + (k & 3) * 32;
-                umma_ss(d_o, sdesc_sw128(pa + a_off, 16, 1024),
-                        sdesc_sw128(v_addr + k * 2048, kSub, 1024), args.idesc_pv,
-                        (jp > 0 || k > 0) ? 1u : 0u);
-              }
-              umma_commit(&pv_done[g * 2 + (t & 1)]);
+              for (int k = 0; k < kTileK / 16; ++k)
+                umma_ts(d_o, pa + k * 8, sdesc_sw128(v_addr + k * 2048, kSub, 1024),
+                        args.idesc_pv, (jp > 0 || k > 0) ? 1u : 0u);
+              umma_commit(&pv_done[g]);
               ++pvc[g];
             }
             if (!ok) break;
@@ -631,7 +635,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       umma_commit(drain);
       mbar_wait_drain(drain, 0);
     }
-  } else if (warp >= 2) {
+  } else {
     // -------------------------------------------------------------- softmax
     const int g = (warp - 2) >> 2;  // group 0: warps 2-5, group 1: warps 6-9
     const int quad = warp & 3;
@@ -640,6 +644,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const uint32_t s_col = static_cast<uint32_t>(g * kTileK);
     const uint32_t o_col = Cfg::kOCol + g * HD;
     const float sl2 = args.scale_log2;
+    const uint32_t p_col = Cfg::kPCol + g * (kTileK / 2);
     uint32_t t = 0;  // tiles this group has processed (all items)
     bool ok = true;
     for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
@@ -687,61 +692,60 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             if (masked) sv[c] = __float_as_uint(-INFINITY);
           }
         }
-        float mx = -INFINITY;
+        // Row max: eight independent three-input max chains, then combine.
+        float pm[8];
 #pragma unroll
-        for (int c = 0; c < kTileK; ++c) mx = fmaxf(mx, __uint_as_float(sv[c]));
+        for (int a = 0; a < 8; ++a) pm[a] = __uint_as_float(sv[a]);
+#pragma unroll
+        for (int c = 8; c < kTileK; c += 16) {
+#pragma unroll
+          for (int a = 0; a < 8; ++a)
+            pm[a] = fmax3(pm[a], __uint_as_float(sv[c + a]), __uint_as_float(sv[c + 8 + a]));
+        }
+        const float mx = fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]),
+                               fmaxf(pm[6], pm[7]));
         const float m_new = fmaxf(m_ref, mx);
-        const bool grow = m_new > m_ref && (m_ref == -INFINITY || (m_new - m_ref) * sl2 > kRescaleLog2);
+        const bool grow =
+            m_new > m_ref && (m_ref == -INFINITY || (m_new - m_ref) * sl2 > kRescaleLog2);
         const float alpha = grow ? fast_exp2((m_ref - m_new) * sl2) : 1.f;
         if (grow) {
           l_i *= alpha;
           m_ref = m_new;
         }
         const float mb = m_ref == -INFINITY ? 0.f : m_ref * sl2;
-        // P buffer (t & 1) is free once the PV of this group's tile t-2 is done.
-        if (t >= 2) {
-          const uint32_t tq = t - 2;
-          w_ok = mbar_wait(&pv_done[g * 2 + (tq & 1)], (tq >> 1) & 1, abort_flag);
-          if (!__all_sync(0xffffffffu, w_ok)) {
-            ok = false;
-            break;
-          }
-        }
-        uint8_t* prow = sP + (g * 2 + (t & 1)) * Cfg::kPBytes + r * 128;
-        float rowsum = 0.f;
+        // Exponentials into registers (64 packed pairs) before P is touched.
+        // Alternate pairs go to the MUFU unit and to a polynomial on the FMA
+        // pipe, which together issue twice the exponentials the MUFU alone
+        // can.  Row sums in fp32 (packed adds, two chains).
+        uint32_t e[kTileK / 2];
+        float sa0 = 0.f, sa1 = 0.f, sb0 = 0.f, sb1 = 0.f;
 #pragma unroll
-        for (int cc = 0; cc < kTileK / 8; ++cc) {
-          float e[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            e[i] = fast_exp2(fmaf(__uint_as_float(sv[cc * 8 + i]), sl2, -mb));
-            rowsum += e[i];
-          }
-          uint4 v;
-          if (args.bf16) {
-            v.x = Pack2<__nv_bfloat16>::pack(e[0], e[1]);
-            v.y = Pack2<__nv_bfloat16>::pack(e[2], e[3]);
-            v.z = Pack2<__nv_bfloat16>::pack(e[4], e[5]);
-            v.w = Pack2<__nv_bfloat16>::pack(e[6], e[7]);
+        for (int c = 0; c < kTileK / 2; ++c) {
+          float x0, x1, p0, p1;
+          ffma2(x0, x1, __uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1]), sl2, -mb);
+          if (c & 1) {
+            exp2_poly2(p0, p1, x0, x1);
+            add2v(sb0, sb1, p0, p1);
           } else {
-            v.x = Pack2<__half>::pack(e[0], e[1]);
-            v.y = Pack2<__half>::pack(e[2], e[3]);
-            v.z = Pack2<__half>::pack(e[4], e[5]);
-            v.w = Pack2<__half>::pack(e[6], e[7]);
+            p0 = fast_exp2(x0);
+            p1 = fast_exp2(x1);
+            add2v(sa0, sa1, p0, p1);
           }
-          const int sub = cc >> 3, c8 = cc & 7;
-          *reinterpret_cast<uint4*>(prow + sub * kSub + ((c8 ^ (r & 7)) << 4)) = v;
+          e[c] = kBF16 ? Pack2<__nv_bfloat16>::pack(p0, p1) : Pack2<__half>::pack(p0, p1);
         }
+        const float rowsum = (sa0 + sa1) + (sb0 + sb1);
         l_i += rowsum;
-        // Rescale O (after the previous PV has landed) before this tile's PV.
-        if (j > 0 && __any_sync(0xffffffffu, grow)) {
-          const uint32_t tp = t - 1;
-          w_ok = mbar_wait(&pv_done[g * 2 + (tp & 1)], (tp >> 1) & 1, abort_flag);
+        // The previous PV has read P and accumulated into O: P is free and O
+        // current.
+        if (t >= 1) {
+          w_ok = mbar_wait(&pv_done[g], (t - 1) & 1, abort_flag);
           if (!__all_sync(0xffffffffu, w_ok)) {
             ok = false;
             break;
           }
           tc_fence_after();
+        }
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {
 #pragma unroll
           for (int c = 0; c < HD / 32; ++c) {
             uint32_t o[32];
@@ -754,16 +758,17 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           }
           tmem_st_wait();
         }
-        fence_proxy_async_smem();
+        tmem_st32p(lane_base + p_col, e);
+        tmem_st32p(lane_base + p_col + 32, e + 32);
+        tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[g * 2 + (t & 1)]);
+        if (lane == 0) mbar_arrive(&p_full[g]);
         ++t;
       }
       if (!ok) break;
       // Epilogue: O / l once the item's last PV has landed.
-      const uint32_t tl = t - 1;
-      const bool w_ok = mbar_wait(&pv_done[g * 2 + (tl & 1)], (tl >> 1) & 1, abort_flag);
+      const bool w_ok = mbar_wait(&pv_done[g], (t - 1) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, w_ok)) break;
       tc_fence_after();
       const float inv_l = l_i > 0.f ? 1.f / l_i : 0.f;
@@ -778,7 +783,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           for (int i = 0; i < 16; ++i) {
             const float x0 = __uint_as_float(o[2 * i]) * inv_l;
             const float x1 = __uint_as_float(o[2 * i + 1]) * inv_l;
-            p[i] = args.bf16 ? Pack2<__nv_bfloat16>::pack(x0, x1) : Pack2<__half>::pack(x0, x1);
+            p[i] = kBF16 ? Pack2<__nv_bfloat16>::pack(x0, x1) : Pack2<__half>::pack(x0, x1);
           }
           uint4* dst = reinterpret_cast<uint4*>(out_ptr + c * 32);
 #pragma unroll
@@ -838,9 +843,11 @@ int launch_attn_pair(const void* qkv, const AttnArgs& args, cudaStream_t stream)
   {
     std::lock_guard<std::mutex> lock(g_pair_attr_mu);
     if (dev < 64 && !g_pair_attr_done[dev]) {
-      if (const int fs = cuda_status(cudaFuncSetAttribute(attn_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(PairCfg::kSmemBytes))))
-        return fs;
+      for (auto fn : {attn_pair_kernel<false>, attn_pair_kernel<true>})
+        if (const int fs = cuda_status(cudaFuncSetAttribute(
+                fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                static_cast<int>(PairCfg::kSmemBytes))))
+          return fs;
       g_pair_attr_done[dev] = true;
     }
   }
@@ -853,7 +860,10 @@ int launch_attn_pair(const void* qkv, const AttnArgs& args, cudaStream_t stream)
   if (st != TJB_OK) return st;
   const long total = static_cast<long>(args.B) * args.H * ((args.S + 2 * kTileQ - 1) / (2 * kTileQ));
   const int grid = static_cast<int>(total < num_sms() ? total : num_sms());
-  attn_pair_kernel<<<grid, kPairThreads, PairCfg::kSmemBytes, stream>>>(tm, args);
+  if (args.bf16)
+    attn_pair_kernel<true><<<grid, kPairThreads, PairCfg::kSmemBytes, stream>>>(tm, args);
+  else
+    attn_pair_kernel<false><<<grid, kPairThreads, PairCfg::kSmemBytes, stream>>>(tm, args);
   return launch_status();
 }
 

@@ -196,6 +196,18 @@ __device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t adesc, uint64_
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]: A (M x K, 16-bit) is read from tensor
+// memory, row i in lane i, two consecutive K elements per 32-bit column.
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05 op this thread issued so far is done.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile(
@@ -232,6 +244,20 @@ __device__ __forceinline__ void tmem_ld32p(uint32_t taddr, uint32_t* r) {
         "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32p(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
 
@@ -286,6 +312,72 @@ struct Pack2<__half> {
     return *reinterpret_cast<uint32_t*>(&v);
   }
 };
+
+// max(a, b, c) in one instruction (sm_100 three-input max).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Two fp32 fused multiply-adds in one packed instruction:
+// (x0, x1) = (a0 * b + c, a1 * b + c).
+__device__ __forceinline__ void ffma2(float& x0, float& x1, float a0, float a1, float b,
+                                      float c) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %4};\n\t"
+      "mov.b64 rc, {%5, %5};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(x0), "=f"(x1)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+
+// Packed fp32 ops on pairs (sm_100 f32x2): (a0, a1) op (b0, b1).
+__device__ __forceinline__ void fma2v(float& d0, float& d1, float a0, float a1, float b0,
+                                      float b1, float c0, float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
+__device__ __forceinline__ void add2v(float& d0, float& d1, float a0, float a1) {
+  asm("{\n\t.reg .b64 ra, rd;\n\t"
+      "mov.b64 rd, {%0, %1};\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "add.rn.f32x2 rd, rd, ra;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a0), "f"(a1));
+}
+
+// 2^x for a pair of arguments on the FMA pipe instead of the MUFU unit.
+// Cody & Waite range reduction: n = round(x) (by adding and subtracting
+// 1.5 * 2^23), f = x - n in [-1/2, 1/2]; 2^f by a degree-3 polynomial whose
+// coefficients were fitted for minimal relative error on [-1/2, 1/2]
+// (max relative error 7.5e-5, below half an fp16 ulp); 2^n enters by adding
+// n to the exponent field.  Arguments are clamped below at -64 (the result
+// is then < 2^-63, i.e. zero once rounded to a 16-bit P).
+__device__ __forceinline__ void exp2_poly2(float& y0, float& y1, float x0, float x1) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x0 = fmaxf(x0, -64.f);
+  x1 = fmaxf(x1, -64.f);
+  float t0, t1, n0, n1, f0, f1, p0, p1;
+  fma2v(t0, t1, x0, x1, 1.f, 1.f, kRound, kRound);    // round(x) in the low mantissa bits
+  fma2v(n0, n1, t0, t1, 1.f, 1.f, -kRound, -kRound);  // round(x) as a float
+  fma2v(f0, f1, n0, n1, -1.f, -1.f, x0, x1);          // f = x - n
+  fma2v(p0, p1, f0, f1, 0.0551716052f, 0.0551716052f, 0.2426111102f, 0.2426111102f);
+  fma2v(p0, p1, p0, p1, f0, f1, 0.6932609677f, 0.6932609677f);
+  fma2v(p0, p1, p0, p1, f0, f1, 0.9999280572f, 0.9999280572f);
+  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+}
 
 // Exact (erf) GELU: 0.5 x (1 + erf(x / sqrt 2)), as F.gelu(approximate="none").
 __device__ __forceinline__ float gelu_erf(float x) {
