@@ -179,17 +179,23 @@ class KernelTimer:
     def __enter__(self):
         K = self.K
 
+        # FLOPs are counted on the rows that carry tokens: all rows without a
+        # tile list, the valid tokens (sum of lengths) when dead tiles are
+        # skipped -- the work the caller asked for, never the rows skipped.
+        def rows_of(a, kwargs):
+            return self.cfg["valid_tokens"] if kwargs.get("m_tiles") is not None else a.shape[0]
+
         def gemm_cost(args, kwargs, out):
             a, w = args[0], args[1]
-            return 2.0 * a.shape[0] * a.shape[1] * w.shape[0], 0.0, 1
+            return 2.0 * rows_of(a, kwargs) * a.shape[1] * w.shape[0], 0.0, 1
 
         def ffn_cost(args, kwargs, out):
             h, w1 = args[0], args[1]
-            return 4.0 * h.shape[0] * h.shape[1] * w1.shape[0], 0.0, 2
+            return 4.0 * rows_of(h, kwargs) * h.shape[1] * w1.shape[0], 0.0, 2
 
         def ln_cost(args, kwargs, out):
             res, delta = args[0], args[1]
-            n = res.numel()
+            n = rows_of(res, kwargs) * res.shape[1]
             nbytes = n * 4 + (0 if delta is None else n * delta.element_size())
             if delta is not None and kwargs.get("write_residual", True):
                 nbytes += n * 4
@@ -207,7 +213,7 @@ class KernelTimer:
 
         for name, cost in (("gemm_bias", gemm_cost), ("fused_ffn", ffn_cost),
                            ("fused_add_layernorm", ln_cost), ("flash_attention", attn_cost),
-                           ("mask_lengths", mask_cost)):
+                           ("mask_lengths", mask_cost), ("row_tiles", mask_cost)):
             self._orig[name] = getattr(K, name)
             setattr(K, name, self._wrap(name, self._orig[name], cost))
         return self
@@ -410,7 +416,7 @@ def main():
                                       label="instrumented"))
         model(x, mask)
         torch.cuda.synchronize(dev)
-        timer = KernelTimer(K, {"lengths": lengths})
+        timer = KernelTimer(K, {"lengths": lengths, "valid_tokens": sum(lengths)})
         with timer:
             for _ in range(ksteps):
                 model(x, mask)

@@ -77,6 +77,17 @@ int tjb_add_layernorm(const float* res, const void* delta, float* res_out, void*
                       tjb_stream_t stream);
 
 /*
+ * tjb_add_layernorm restricted to the live 128-row tiles listed in m_tiles
+ * (device int32: m_tiles[0] = count, then tile indices; see tjb_row_tiles).
+ * Rows of unlisted tiles are neither read nor written.  m_tiles == NULL
+ * processes every row.  Padding-aware form of the same facade function.
+ */
+int tjb_add_layernorm_tiles(const float* res, const void* delta, float* res_out, void* out,
+                            const float* w, const float* b, int64_t rows, int d, float eps,
+                            int delta_dtype, int out_dtype, const uint8_t* row_mask,
+                            const int32_t* m_tiles, tjb_stream_t stream);
+
+/*
  * C[M, N] = act(A[M, K] * B[N, K]^T + bias[N])   on tcgen05 tensor cores.
  * A, B: f16 or bf16 (same type), K-major (K contiguous; B is the nn.Linear
  * weight layout [out, in]).  bias: fp32 [N] or NULL.  act: 0 = none,
@@ -90,6 +101,17 @@ int tjb_add_layernorm(const float* res, const void* delta, float* res_out, void*
 int tjb_gemm_bias(const void* A, const void* B, const float* bias, void* C,
                   int M, int N, int K, int lda, int ldb, int ldc,
                   int in_dtype, int out_dtype, int act, tjb_stream_t stream);
+
+/*
+ * tjb_gemm_bias computing only the 128-row M tiles listed in m_tiles (device
+ * int32: m_tiles[0] = count, then tile indices; see tjb_row_tiles); rows of
+ * unlisted tiles of C are not written.  m_tiles == NULL computes all rows.
+ * Padding-aware form of the engine.py:245,247 addmm calls.
+ */
+int tjb_gemm_bias_tiles(const void* A, const void* B, const float* bias, void* C,
+                        int M, int N, int K, int lda, int ldb, int ldc,
+                        int in_dtype, int out_dtype, int act, const int32_t* m_tiles,
+                        tjb_stream_t stream);
 
 /*
  * Causal (or full) multi-head attention forward on tcgen05 tensor cores,
@@ -125,6 +147,11 @@ int tjb_ffn(const void* h, const void* w1, const float* b1, const void* w2,
             const float* b2, void* out, void* hidden, int T, int d, int F,
             int in_dtype, int out_dtype, tjb_stream_t stream);
 
+/* tjb_ffn over the live 128-row tiles listed in m_tiles (see tjb_row_tiles). */
+int tjb_ffn_tiles(const void* h, const void* w1, const float* b1, const void* w2,
+                  const float* b2, void* out, void* hidden, int T, int d, int F,
+                  int in_dtype, int out_dtype, const int32_t* m_tiles, tjb_stream_t stream);
+
 /*
  * tjb_ffn without any device allocation and without caller scratch: the
  * [T, F] hidden activations live in a 16 MiB device array inside the library
@@ -152,6 +179,21 @@ int tjb_ffn_noalloc(const void* h, const void* w1, const float* b1, const void* 
  */
 int tjb_mask_lengths(const uint8_t* mask, int B, int S, int32_t* lengths,
                      int32_t* flags, tjb_stream_t stream);
+
+/*
+ * Live 128-row tiles of the flattened [B*S] token axis for a prefix padding
+ * mask, on the device (no host synchronisation): a tile is live when it holds
+ * a row (b, s) with s < round_up(lengths[b], 128) -- every valid row plus the
+ * padded rows that share the last 128-key attention tile of a sequence.  With
+ * flags pointing at a non-zero word (a non-prefix mask) or lengths == NULL,
+ * every tile is live.  tiles: int32 [1 + ceil(B*S/128)]; tiles[0] = count.
+ * Padded rows never influence valid rows (row-wise ops; attention masks or
+ * never loads padded keys), so the forward may skip dead tiles and zero the
+ * padded rows once at the end.  No counterpart in the reference (it computes
+ * every row and zeroes padding after each block, engine.py:267-268).
+ */
+int tjb_row_tiles(const int32_t* lengths, const int32_t* flags, int B, int S, int32_t* tiles,
+                  tjb_stream_t stream);
 
 /*
  * Text of the last CUDA error this library saw on the calling thread (the

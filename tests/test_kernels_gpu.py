@@ -230,3 +230,62 @@ def test_bounded_wait_times_out_and_reports():
     # The context is still usable afterwards.
     x = torch.randn(128, 64, device=DEV).bfloat16()
     assert torch.isfinite(K().gemm_bias(x, x[:64], None)).all()
+
+
+# ------------------------------------------------------- padding-aware tiles
+
+def row_tiles_reference(lengths, b, s):
+    """Live 128-row tiles: those holding a row (b, s) with s < round_up(len, 128)."""
+    t = b * s
+    live = []
+    for tile in range((t + 127) // 128):
+        r0, r1 = tile * 128, min(tile * 128 + 128, t)
+        if any((r % s) < (min(lengths[r // s], s) + 127) // 128 * 128 for r in range(r0, r1)):
+            live.append(tile)
+    return live
+
+
+@pytest.mark.parametrize("b,s,lens", [(4, 1024, [1024, 1, 300, 0]), (3, 200, [200, 17, 129]),
+                                      (5, 37, [1, 37, 20, 0, 5]), (2, 4096, [2048, 4000])])
+def test_row_tiles(b, s, lens):
+    lengths = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    tiles = K().row_tiles(lengths, flags, b, s, torch.device(DEV)).cpu().tolist()
+    expect = row_tiles_reference(lens, b, s)
+    assert tiles[0] == len(expect) and tiles[1:1 + tiles[0]] == expect
+    flags.fill_(9)  # non-prefix mask: every tile is live
+    tiles = K().row_tiles(lengths, flags, b, s, torch.device(DEV)).cpu().tolist()
+    n = (b * s + 127) // 128
+    assert tiles[0] == n and tiles[1:1 + n] == list(range(n))
+
+
+def test_gemm_and_layernorm_visit_only_listed_tiles():
+    m, n, k = 1000, 512, 256
+    a = torch.randn(m, k, device=DEV).half()
+    w = (torch.randn(n, k, device=DEV) / 16).half()
+    bias = torch.randn(n, device=DEV)
+    listed = [0, 2, 7]  # tile 7 is the ragged last tile (rows 896..999)
+    tiles = torch.tensor([len(listed)] + listed + [0] * 5, dtype=torch.int32, device=DEV)
+    out = torch.full((m, n), 7.0, dtype=torch.float32, device=DEV)
+    K().gemm_bias(a, w, bias, out_dtype=torch.float32, out=out, m_tiles=tiles)
+    ref = a.double() @ w.double().T + bias.double()
+    for t in range(8):
+        rows = slice(t * 128, min(t * 128 + 128, m))
+        if t in listed:
+            assert (out[rows].double() - ref[rows]).abs().max().item() < 1e-3
+        else:
+            assert (out[rows] == 7.0).all()
+    res = torch.randn(m, 1024, device=DEV)
+    delta = torch.randn(m, 1024, device=DEV)
+    w1, b1 = torch.randn(1024, device=DEV), torch.randn(1024, device=DEV)
+    res0 = res.clone()
+    new_res, h = K().fused_add_layernorm(res, delta, w1, b1, 1e-5, out_dtype=torch.float32,
+                                         residual_out=res, m_tiles=tiles)
+    ref_h = F.layer_norm(res0 + delta, (1024,), w1, b1, 1e-5)
+    for t in range(8):
+        rows = slice(t * 128, min(t * 128 + 128, m))
+        if t in listed:
+            assert (h[rows] - ref_h[rows]).abs().max().item() < 1e-4
+            assert torch.equal(new_res[rows], (res0 + delta)[rows])
+        else:
+            assert torch.equal(new_res[rows], res0[rows])

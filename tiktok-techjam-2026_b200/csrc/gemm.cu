@@ -9,7 +9,8 @@
 //   warps 2..5  epilogue: tcgen05.ld the accumulator (one TMEM lane = one
 //               output row per thread), add bias, optional erf-GELU, convert,
 //               store; then hand the accumulator buffer back to the MMA warp.
-// The epilogue of tile i overlaps the main loop of tile i+1.  Output tiles are
+// The epilogue of tile i overlaps the main loop of tile i+1.  With a list of
+// live M tiles (padding-aware forward), only those row tiles are visited.  Output tiles are
 // visited in groups of 16 M-blocks so the CTAs resident at one time share
 // both A rows and B columns in L2.
 #include <mutex>
@@ -35,6 +36,9 @@ struct GemmCfg {
 
 struct GemmArgs {
   const float* bias;
+  // Optional list of live 128-row M tiles: m_tiles[0] = count, then the
+  // tile indices.  Tiles not listed are neither computed nor written.
+  const int32_t* m_tiles;
   void* C;
   int M, N, K, ldc;
   int out_dtype;
@@ -126,7 +130,7 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_m = (args.M + kBM - 1) / kBM;
+  const int num_m = args.m_tiles != nullptr ? __ldg(args.m_tiles) : (args.M + kBM - 1) / kBM;
   const int num_n = (args.N + BN - 1) / BN;
   const int num_k = (args.K + kBK - 1) / kBK;
   const int num_tiles = num_m * num_n;
@@ -164,6 +168,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int m_blk, n_blk;
         tile_coords(t, num_m, num_n, m_blk, n_blk);
+        if (args.m_tiles != nullptr) m_blk = __ldg(args.m_tiles + 1 + m_blk);
         for (int kb = 0; kb < num_k; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
             ok = false;
@@ -233,6 +238,7 @@ __global__ void __launch_bounds__(192, 1)
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       int m_blk, n_blk;
       tile_coords(t, num_m, num_n, m_blk, n_blk);
+      if (args.m_tiles != nullptr) m_blk = __ldg(args.m_tiles + 1 + m_blk);
       bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
@@ -306,9 +312,10 @@ int launch_gemm(const void* A, const void* B, const GemmArgs& args, int lda, int
 }  // namespace
 }  // namespace tjb
 
-extern "C" int tjb_gemm_bias(const void* A, const void* B, const float* bias, void* C, int M,
-                             int N, int K, int lda, int ldb, int ldc, int in_dtype, int out_dtype,
-                             int act, tjb_stream_t stream) {
+extern "C" int tjb_gemm_bias_tiles(const void* A, const void* B, const float* bias, void* C,
+                                   int M, int N, int K, int lda, int ldb, int ldc, int in_dtype,
+                                   int out_dtype, int act, const int32_t* m_tiles,
+                                   tjb_stream_t stream) {
   using namespace tjb;
   if (!A || !B || !C || M < 0 || N <= 0 || K <= 0) return TJB_ERR_INVALID_ARGUMENT;
   if (in_dtype != TJB_F16 && in_dtype != TJB_BF16) return TJB_ERR_UNSUPPORTED_DTYPE;
@@ -323,6 +330,7 @@ extern "C" int tjb_gemm_bias(const void* A, const void* B, const float* bias, vo
   const bool bf16 = in_dtype == TJB_BF16;
   GemmArgs args;
   args.bias = bias;
+  args.m_tiles = m_tiles;
   args.C = C;
   args.M = M;
   args.N = N;
@@ -345,4 +353,11 @@ extern "C" int tjb_gemm_bias(const void* A, const void* B, const float* bias, vo
   }
   args.idesc = idesc_f16(kBM, 64, bf16, false);
   return launch_gemm<64>(A, B, args, lda, ldb, bf16, s);
+}
+
+extern "C" int tjb_gemm_bias(const void* A, const void* B, const float* bias, void* C, int M,
+                             int N, int K, int lda, int ldb, int ldc, int in_dtype, int out_dtype,
+                             int act, tjb_stream_t stream) {
+  return tjb_gemm_bias_tiles(A, B, bias, C, M, N, K, lda, ldb, ldc, in_dtype, out_dtype, act,
+                             nullptr, stream);
 }

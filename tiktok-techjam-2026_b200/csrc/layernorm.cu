@@ -73,18 +73,28 @@ __device__ __forceinline__ float row_sum(float v, float* scratch) {
 
 constexpr int kBlock = 256;
 constexpr int kMaxChunks = 8;
+constexpr int kTileRows = 128;  // row-tile granularity of the live-tile list
 
 template <int TPR>
 __global__ void __launch_bounds__(kBlock) add_layernorm_kernel(
     const float* res, const void* __restrict__ delta, float* res_out, void* out,
     const float* __restrict__ w, const float* __restrict__ b, int64_t rows, int d, float eps,
-    int delta_dtype, int out_dtype, const uint8_t* __restrict__ row_mask) {
+    int delta_dtype, int out_dtype, const uint8_t* __restrict__ row_mask,
+    const int32_t* __restrict__ m_tiles) {
   static_assert(TPR == 32 || TPR == 128 || TPR == 256, "threads per row");
   constexpr int kRowsPerBlock = kBlock / TPR;
   __shared__ float scratch[kBlock / 32];
 
   const int t = threadIdx.x % TPR;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + threadIdx.x / TPR;
+  int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + threadIdx.x / TPR;
+  if (m_tiles != nullptr) {
+    // Blocks walk the listed 128-row tiles only (uniform per block).
+    constexpr int kBlocksPerTile = kTileRows / kRowsPerBlock;
+    const int li = blockIdx.x / kBlocksPerTile;
+    if (li >= __ldg(m_tiles)) return;
+    row = static_cast<int64_t>(__ldg(m_tiles + 1 + li)) * kTileRows +
+          (blockIdx.x % kBlocksPerTile) * kRowsPerBlock + threadIdx.x / TPR;
+  }
   const bool active = row < rows;
   const int64_t base = row * d;
 
@@ -144,10 +154,11 @@ __global__ void __launch_bounds__(kBlock) add_layernorm_kernel(
 }  // namespace
 }  // namespace tjb
 
-extern "C" int tjb_add_layernorm(const float* res, const void* delta, float* res_out, void* out,
-                                 const float* w, const float* b, int64_t rows, int d, float eps,
-                                 int delta_dtype, int out_dtype, const uint8_t* row_mask,
-                                 tjb_stream_t stream) {
+extern "C" int tjb_add_layernorm_tiles(const float* res, const void* delta, float* res_out,
+                                       void* out, const float* w, const float* b, int64_t rows,
+                                       int d, float eps, int delta_dtype, int out_dtype,
+                                       const uint8_t* row_mask, const int32_t* m_tiles,
+                                       tjb_stream_t stream) {
   using namespace tjb;
   if (!res || !out || !w || !b || rows < 0 || d <= 0) return TJB_ERR_INVALID_ARGUMENT;
   if (d % 4 != 0 || d > 8192) return TJB_ERR_BAD_SHAPE;
@@ -161,17 +172,29 @@ extern "C" int tjb_add_layernorm(const float* res, const void* delta, float* res
   if (!device_ok()) return TJB_ERR_NO_DEVICE;
   if (rows == 0) return TJB_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // With a tile list the grid covers every 128-row tile; blocks past the
+  // list's count exit at once.
+  const int64_t tiles = (rows + kTileRows - 1) / kTileRows;
   if (d <= 1024) {
-    const int64_t grid = (rows + (kBlock / 32) - 1) / (kBlock / 32);
+    const int64_t grid = m_tiles ? tiles * (kTileRows / 8) : (rows + 7) / 8;
     add_layernorm_kernel<32><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
-        res, delta, res_out, out, w, b, rows, d, eps, delta_dtype, out_dtype, row_mask);
+        res, delta, res_out, out, w, b, rows, d, eps, delta_dtype, out_dtype, row_mask, m_tiles);
   } else if (d <= 4096) {
-    const int64_t grid = (rows + (kBlock / 128) - 1) / (kBlock / 128);
+    const int64_t grid = m_tiles ? tiles * (kTileRows / 2) : (rows + 1) / 2;
     add_layernorm_kernel<128><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
-        res, delta, res_out, out, w, b, rows, d, eps, delta_dtype, out_dtype, row_mask);
+        res, delta, res_out, out, w, b, rows, d, eps, delta_dtype, out_dtype, row_mask, m_tiles);
   } else {
-    add_layernorm_kernel<256><<<static_cast<unsigned>(rows), kBlock, 0, s>>>(
-        res, delta, res_out, out, w, b, rows, d, eps, delta_dtype, out_dtype, row_mask);
+    const int64_t grid = m_tiles ? tiles * kTileRows : rows;
+    add_layernorm_kernel<256><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
+        res, delta, res_out, out, w, b, rows, d, eps, delta_dtype, out_dtype, row_mask, m_tiles);
   }
   return launch_status();
+}
+
+extern "C" int tjb_add_layernorm(const float* res, const void* delta, float* res_out, void* out,
+                                 const float* w, const float* b, int64_t rows, int d, float eps,
+                                 int delta_dtype, int out_dtype, const uint8_t* row_mask,
+                                 tjb_stream_t stream) {
+  return tjb_add_layernorm_tiles(res, delta, res_out, out, w, b, rows, d, eps, delta_dtype,
+                                 out_dtype, row_mask, nullptr, stream);
 }

@@ -125,6 +125,59 @@ __global__ void __launch_bounds__(1024) mask_lengths_kernel(const uint8_t* __res
   if (threadIdx.x == 0) *flags = any_step ? TJB_ERR_NON_PREFIX_MASK : 0;
 }
 
+// --------------------------------------------------------------- row tiles
+// Live 128-row tiles of the flattened [B*S] token axis.  A tile is live when
+// it holds a row (b, s) with s < round_up(lengths[b], 128): every valid row,
+// plus the padded rows that share the valid rows' last 128-key attention
+// tile (attention reads those keys, masked, so they must stay finite).  With
+// a non-prefix mask (flags != 0) or no lengths every tile is live.
+// tiles[0] = count, tiles[1..] = tile indices in increasing order.
+__global__ void __launch_bounds__(1024) row_tiles_kernel(const int32_t* __restrict__ lengths,
+                                                         const int32_t* __restrict__ flags,
+                                                         int B, int S, int32_t* __restrict__ tiles) {
+  __shared__ int s_warp[32];
+  __shared__ int s_base;
+  const int64_t T = static_cast<int64_t>(B) * S;
+  const int n_tiles = static_cast<int>((T + 127) / 128);
+  const bool all = lengths == nullptr || (flags != nullptr && __ldg(flags) != 0);
+  if (threadIdx.x == 0) s_base = 0;
+  __syncthreads();
+  for (int t0 = 0; t0 < n_tiles; t0 += blockDim.x) {
+    const int t = t0 + threadIdx.x;
+    int live = 0;
+    if (t < n_tiles) {
+      if (all) {
+        live = 1;
+      } else {
+        const int64_t r0 = static_cast<int64_t>(t) * 128;
+        const int64_t r1 = min(r0 + 128, T);
+        for (int64_t b = r0 / S; b * S < r1 && !live; ++b) {
+          const int64_t first = max(r0, b * S) - b * S;  // first row of b inside the tile
+          const int len = min(max(__ldg(lengths + b), 0), S);
+          const int64_t reach = (static_cast<int64_t>(len) + 127) / 128 * 128;
+          if (first < reach) live = 1;
+        }
+      }
+    }
+    // Block-wide exclusive scan of the live flags.
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const unsigned ballot = __ballot_sync(0xffffffffu, live);
+    const int in_warp = __popc(ballot & ((1u << lane) - 1u));
+    if (lane == 0) s_warp[warp] = __popc(ballot);
+    __syncthreads();
+    int before = 0, total = 0;
+    for (int w = 0; w < (blockDim.x >> 5); ++w) {
+      if (w < warp) before += s_warp[w];
+      total += s_warp[w];
+    }
+    if (live) tiles[1 + s_base + before + in_warp] = t;
+    __syncthreads();
+    if (threadIdx.x == 0) s_base += total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) tiles[0] = s_base;
+}
+
 // --------------------------------------------------------- bounded-wait test
 __global__ void selftest_wait_kernel(const int32_t* flag, int64_t timeout_ns) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
@@ -185,6 +238,15 @@ int tjb_mask_lengths(const uint8_t* mask, int B, int S, int32_t* lengths, int32_
   if (!tjb::device_ok()) return TJB_ERR_NO_DEVICE;
   tjb::mask_lengths_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       mask, B, S, lengths, flags);
+  return tjb::launch_status();
+}
+
+int tjb_row_tiles(const int32_t* lengths, const int32_t* flags, int B, int S, int32_t* tiles,
+                  tjb_stream_t stream) {
+  if (!tiles || B <= 0 || S <= 0) return TJB_ERR_INVALID_ARGUMENT;
+  if (!tjb::device_ok()) return TJB_ERR_NO_DEVICE;
+  tjb::row_tiles_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(lengths, flags,
+                                                                                B, S, tiles);
   return tjb::launch_status();
 }
 

@@ -24,12 +24,19 @@ SIGNATURES = {
     "tjb_last_cuda_error": (ctypes.c_char_p, []),
     "tjb_add_layernorm": (_c_int, [_p, _p, _p, _p, _p, _p, _c_i64, _c_int, _c_f32,
                                    _c_int, _c_int, _p, _p]),
+    "tjb_add_layernorm_tiles": (_c_int, [_p, _p, _p, _p, _p, _p, _c_i64, _c_int, _c_f32,
+                                         _c_int, _c_int, _p, _p, _p]),
     "tjb_gemm_bias": (_c_int, [_p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int,
                                _c_int, _c_int, _c_int, _c_int, _p]),
+    "tjb_gemm_bias_tiles": (_c_int, [_p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                     _c_int, _c_int, _c_int, _c_int, _p, _p]),
     "tjb_flash_fwd": (_c_int, [_p, _p, _c_int, _c_int, _c_int, _c_int, _c_f32, _c_int,
                                _p, _p, _p, _c_int, _p]),
     "tjb_ffn": (_c_int, [_p, _p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int,
                          _c_int, _p]),
+    "tjb_ffn_tiles": (_c_int, [_p, _p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int,
+                               _c_int, _p, _p]),
+    "tjb_row_tiles": (_c_int, [_p, _p, _c_int, _c_int, _p, _p]),
     "tjb_ffn_noalloc": (_c_int, [_p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int,
                                  _c_int, _p]),
     "tjb_mask_lengths": (_c_int, [_p, _c_int, _c_int, _p, _p, _p]),

@@ -23,7 +23,10 @@ synchronisation at all, unlike the reference's memoised ``.item()`` calls
 length and stop keys at it; any other mask is applied key by key inside the
 attention kernel (the reference routed that case to SDPA with a bias).
 Padded rows never influence valid rows (row-wise ops, masked keys), so they
-are zeroed once, by the final LayerNorm.
+are zeroed once, by the final LayerNorm -- and with a prefix mask the
+LayerNorms and GEMMs skip every 128-row tile that holds no row attention can
+read (``tjb_row_tiles``; plan knob ``skip_padding``), so a half-padded batch
+costs about half the work.
 """
 
 from __future__ import annotations
@@ -130,11 +133,13 @@ class Engine:
         tokens = batch * seq
         heads, hd = self.num_heads, self.head_dim
 
-        mask_u8 = lengths = flags = None
+        mask_u8 = lengths = flags = tiles = None
         if mask is not None:
             mask_u8 = mask.contiguous().view(torch.uint8) if mask.dtype == torch.bool \
                 else (mask != 0).to(torch.uint8)
             lengths, flags = K.mask_lengths(mask_u8)
+            if plan.skip_padding:
+                tiles = K.row_tiles(lengths, flags, batch, seq, x.device)
 
         res = x.reshape(tokens, d)
         if res.dtype != torch.float32 or not res.is_contiguous():
@@ -144,18 +149,20 @@ class Engine:
         for lw in self.layers:
             res, h = K.fused_add_layernorm(
                 res, pending, lw.ln1_w, lw.ln1_b, lw.ln1_eps, out_dtype=plan.compute_dtype,
-                residual_out=res if (own_res and pending is not None) else None)
+                residual_out=res if (own_res and pending is not None) else None,
+                m_tiles=tiles)
             own_res = own_res or pending is not None
-            qkv = K.gemm_bias(h, lw.wqkv, lw.bqkv)
+            qkv = K.gemm_bias(h, lw.wqkv, lw.bqkv, m_tiles=tiles)
             ctx = K.flash_attention(qkv.view(batch, seq, 3, heads, hd), heads,
                                     causal=self.causal, lengths=lengths, key_mask=mask_u8,
                                     mask_flags=flags, scale=self.scale)
-            attn_out = K.gemm_bias(ctx, lw.wo, lw.bo, out_dtype=plan.delta_dtype)
+            attn_out = K.gemm_bias(ctx, lw.wo, lw.bo, out_dtype=plan.delta_dtype, m_tiles=tiles)
             res, h2 = K.fused_add_layernorm(
                 res, attn_out, lw.ln2_w, lw.ln2_b, lw.ln2_eps, out_dtype=plan.compute_dtype,
-                residual_out=res if own_res else None)
+                residual_out=res if own_res else None, m_tiles=tiles)
             own_res = True
-            pending = K.fused_ffn(h2, lw.w1, lw.b1, lw.w2, lw.b2, out_dtype=plan.delta_dtype)
+            pending = K.fused_ffn(h2, lw.w1, lw.b1, lw.w2, lw.b2, out_dtype=plan.delta_dtype,
+                                  m_tiles=tiles)
 
         fw, fb, feps = self.final_ln
         _, out = K.fused_add_layernorm(res, pending, fw, fb, feps, out_dtype=self.dtype,

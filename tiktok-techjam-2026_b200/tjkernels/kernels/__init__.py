@@ -59,6 +59,7 @@ def fused_add_layernorm(
     write_residual: bool = True,
     row_mask: Optional[torch.Tensor] = None,
     residual_out: Optional[torch.Tensor] = None,
+    m_tiles: Optional[torch.Tensor] = None,
 ) -> Tuple[torch.Tensor, torch.Tensor]:
     """``x = residual + delta``; return ``(x, layernorm(x))``.
 
@@ -66,7 +67,8 @@ def fused_add_layernorm(
     With ``write_residual=False`` the sum is not stored and the first result
     is ``residual`` itself.  ``residual_out`` (may alias ``residual``) receives
     the sum instead of a fresh tensor.  Rows with ``row_mask == 0`` (uint8)
-    get an exactly-zero normalised output.
+    get an exactly-zero normalised output.  With ``m_tiles`` (from
+    ``row_tiles``) only the live 128-row tiles are read and written.
     """
     _need_cuda(residual, delta, weight, bias, row_mask)
     if residual.dtype != torch.float32:
@@ -79,10 +81,10 @@ def fused_add_layernorm(
         res_out = residual_out if residual_out is not None else torch.empty_like(residual)
     if delta is not None and not delta.is_contiguous():
         delta = delta.contiguous()
-    status = _lib.lib().tjb_add_layernorm(
+    status = _lib.lib().tjb_add_layernorm_tiles(
         _ptr(residual), _ptr(delta), _ptr(res_out), _ptr(out), _ptr(weight), _ptr(bias),
         rows, d, float(eps), _code(delta.dtype) if delta is not None else _lib.TJB_F32,
-        _code(out_dtype), _ptr(row_mask), _stream(residual.device))
+        _code(out_dtype), _ptr(row_mask), _ptr(m_tiles), _stream(residual.device))
     _lib.check(status, "tjb_add_layernorm")
     return (res_out if res_out is not None else residual), out
 
@@ -95,9 +97,11 @@ def layernorm(x, weight, bias, eps, out_dtype=None):
 
 def gemm_bias(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],
               act: int = ACT_NONE, out_dtype: Optional[torch.dtype] = None,
-              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+              out: Optional[torch.Tensor] = None,
+              m_tiles: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``act(a @ w.T + bias)``: a ``[M, K]``, w ``[N, K]`` (nn.Linear layout),
-    both fp16 or both bf16; bias fp32 ``[N]``; fp32 accumulation."""
+    both fp16 or both bf16; bias fp32 ``[N]``; fp32 accumulation.  With
+    ``m_tiles`` only the listed 128-row tiles of the output are computed."""
     _need_cuda(a, w, bias)
     m, k = a.shape
     n, k2 = w.shape
@@ -108,25 +112,27 @@ def gemm_bias(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],
     out_dtype = out_dtype or a.dtype
     if out is None:
         out = torch.empty((m, n), dtype=out_dtype, device=a.device)
-    status = _lib.lib().tjb_gemm_bias(
+    status = _lib.lib().tjb_gemm_bias_tiles(
         _ptr(a), _ptr(w), _ptr(bias), _ptr(out), m, n, k, a.stride(0), w.stride(0),
-        out.stride(0), _code(a.dtype), _code(out.dtype), act, _stream(a.device))
+        out.stride(0), _code(a.dtype), _code(out.dtype), act, _ptr(m_tiles), _stream(a.device))
     _lib.check(status, "tjb_gemm_bias")
     return out
 
 
 def fused_ffn(h: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor, w2: torch.Tensor,
-              b2: torch.Tensor, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
-    """``gelu_erf(h @ w1.T + b1) @ w2.T + b2``; w1 ``[F, d]``, w2 ``[d, F]``."""
+              b2: torch.Tensor, out_dtype: Optional[torch.dtype] = None,
+              m_tiles: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``gelu_erf(h @ w1.T + b1) @ w2.T + b2``; w1 ``[F, d]``, w2 ``[d, F]``;
+    with ``m_tiles`` only the listed 128-row tiles are computed."""
     _need_cuda(h, w1, b1, w2, b2)
     t, d = h.shape
     f = w1.shape[0]
     out_dtype = out_dtype or h.dtype
     out = torch.empty((t, d), dtype=out_dtype, device=h.device)
     hidden = torch.empty((t, f), dtype=h.dtype, device=h.device)
-    status = _lib.lib().tjb_ffn(
+    status = _lib.lib().tjb_ffn_tiles(
         _ptr(h), _ptr(w1), _ptr(b1), _ptr(w2), _ptr(b2), _ptr(out), _ptr(hidden), t, d, f,
-        _code(h.dtype), _code(out_dtype), _stream(h.device))
+        _code(h.dtype), _code(out_dtype), _ptr(m_tiles), _stream(h.device))
     _lib.check(status, "tjb_ffn")
     return out
 
@@ -174,6 +180,18 @@ def mask_lengths(mask: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     return lengths, flags
 
 
+def row_tiles(lengths: Optional[torch.Tensor], flags: Optional[torch.Tensor], batch: int,
+              seq: int, device: torch.device) -> torch.Tensor:
+    """Device-side list of live 128-row tiles of the [B*S] token axis:
+    int32 ``[1 + ceil(B*S/128)]``, element 0 the count (see tjb_row_tiles)."""
+    _need_cuda(lengths, flags)
+    tiles = torch.empty((1 + (batch * seq + 127) // 128,), dtype=torch.int32, device=device)
+    status = _lib.lib().tjb_row_tiles(_ptr(lengths), _ptr(flags), batch, seq, _ptr(tiles),
+                                      _stream(device))
+    _lib.check(status, "tjb_row_tiles")
+    return tiles
+
+
 def device_status(clear: bool = False) -> int:
     """The device status word (0, or TJB_ERR_DEVICE_TIMEOUT); synchronises."""
     return int(_lib.lib().tjb_device_status(int(clear)))
@@ -181,5 +199,5 @@ def device_status(clear: bool = False) -> int:
 
 __all__ = [
     "ACT_NONE", "ACT_GELU", "fused_add_layernorm", "layernorm", "gemm_bias", "fused_ffn",
-    "flash_attention", "flash_supports", "mask_lengths", "device_status",
+    "flash_attention", "flash_supports", "mask_lengths", "row_tiles", "device_status",
 ]

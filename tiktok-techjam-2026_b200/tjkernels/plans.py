@@ -45,6 +45,9 @@ class Plan:
     delta_dtype: torch.dtype = torch.float32
     # Whole-forward CUDA graph replay.
     cuda_graph: bool = True
+    # Skip the GEMM / LayerNorm work of 128-row tiles that hold only padding
+    # (prefix masks); padded rows still come out exactly zero.
+    skip_padding: bool = True
     label: str = "default"
 
     def to_json(self) -> Dict[str, object]:
@@ -53,6 +56,7 @@ class Plan:
             "residual_dtype": _DTYPE_NAMES[self.residual_dtype],
             "delta_dtype": _DTYPE_NAMES[self.delta_dtype],
             "cuda_graph": self.cuda_graph,
+            "skip_padding": self.skip_padding,
             "label": self.label,
         }
 
@@ -129,6 +133,8 @@ def select_plan(batch: int, seq: int, d_model: int, heads: int, ffn_dim: int, la
     forced = os.environ.get("TJ_COMPUTE_DTYPE")
     if forced in ("float16", "bfloat16"):
         plan = replace(plan, compute_dtype=_DTYPES[forced])
+    if os.environ.get("TJ_NO_SKIP") == "1":
+        plan = replace(plan, skip_padding=False)
     forced = os.environ.get("TJ_DELTA_DTYPE")
     if forced in _DTYPES:
         plan = replace(plan, delta_dtype=_DTYPES[forced])
