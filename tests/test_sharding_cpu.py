@@ -1,0 +1,81 @@
+"""Batch sharding across ranks (CPU, gloo, world size 2).
+
+Sequences are independent in the encoder (row-wise GEMMs and LayerNorms,
+attention within a sequence), so the multi-GPU forward shards the batch with
+no collective: each rank runs its contiguous slice and the results
+concatenate to the single-process forward.  Checked here with the CPU oracle
+on two gloo ranks, plus the host-side shard arithmetic.
+"""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle.model import ModelConfig, build_model, generate_case, oracle_forward
+
+
+def test_shard_range_covers_batch():
+    from tjkernels.parallel import shard_range
+    for batch in (1, 7, 8, 64):
+        for world in (1, 2, 3, 8):
+            spans = [shard_range(batch, world, r) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == batch
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            sizes = [e - s for s, e in spans]
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        shard_range(8, 2, 2)
+
+
+def test_balanced_shards_balance_causal_work():
+    from tjkernels.parallel import balanced_shards
+    lengths = [2048, 1024, 1500, 1100, 2000, 1300, 1800, 1024]
+    shards = balanced_shards(lengths, 4)
+    assert sorted(i for s in shards for i in s) == list(range(8))
+    load = [sum(lengths[i] * (lengths[i] + 1) / 2 + lengths[i] for i in s) for s in shards]
+    assert max(load) / min(load) < 1.5
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, cfg, seed, pad, out_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from tjkernels.parallel import shard_range
+        torch.set_num_threads(1)
+        model = build_model(cfg, 0)
+        x, mask = generate_case(cfg, seed, pad)
+        lo, hi = shard_range(cfg.batch_size, world, rank)
+        local = oracle_forward(model, x[lo:hi], mask[lo:hi])
+        # Shards differ by at most one sequence: gather padded to the largest.
+        spans = [shard_range(cfg.batch_size, world, r) for r in range(world)]
+        most = max(e - s for s, e in spans)
+        padded = torch.zeros(most, cfg.seq_len, cfg.d_model)
+        padded[: hi - lo] = local
+        parts = [torch.empty_like(padded) for _ in range(world)]
+        dist.all_gather(parts, padded)
+        if rank == 0:
+            torch.save(torch.cat([p[: e - s] for p, (s, e) in zip(parts, spans)]), out_path)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_batch_shard_equals_full_forward(tmp_path):
+    cfg = ModelConfig(5, 48, 128, 2, 256, 2, True)
+    out_path = str(tmp_path / "gathered.pt")
+    mp.start_processes(_rank_main, args=(2, _free_port(), cfg, 7, 0.5, out_path), nprocs=2,
+                       join=True, start_method="spawn")
+    gathered = torch.load(out_path)
+    model = build_model(cfg, 0)
+    x, mask = generate_case(cfg, 7, 0.5)
+    full = oracle_forward(model, x, mask)
+    assert (gathered - full).abs().max().item() < 1e-5
