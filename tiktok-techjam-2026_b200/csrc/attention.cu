@@ -94,21 +94,6 @@ __global__ void __launch_bounds__(192, 1)
   const int q_tile = num_q_tiles - 1 - static_cast<int>(blockIdx.y);  // longest rows first
   const int q0 = q_tile * kTileQ;
 
-  // Visible key range and skipping decided from the padding description.
-  const bool prefix = args.lengths != nullptr &&
-                      (args.mask_flags == nullptr || __ldg(args.mask_flags) == 0);
-  const bool use_key_mask = args.key_mask != nullptr && !prefix;
-  int kv_len = args.S;
-  bool skip = false;
-  if (prefix) {
-    const int len = __ldg(args.lengths + b);
-    kv_len = min(max(len, 0), args.S);
-    skip = q0 >= kv_len;
-  }
-  int n_kv = (kv_len + kTileK - 1) / kTileK;
-  if (args.causal) n_kv = min(n_kv, (q0 + kTileQ + kTileK - 1) / kTileK);
-  if (skip) n_kv = 0;
-
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < kStages; ++s) {
@@ -133,6 +118,20 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Visible key range and skipping decided from the padding description.
+  const bool prefix = args.lengths != nullptr &&
+                      (args.mask_flags == nullptr || __ldg(args.mask_flags) == 0);
+  const bool use_key_mask = args.key_mask != nullptr && !prefix;
+  int kv_len = args.S;
+  bool skip = false;
+  if (prefix) {
+    const int len = __ldg(args.lengths + b);
+    kv_len = min(max(len, 0), args.S);
+    skip = q0 >= kv_len;
+  }
+  int n_kv = (kv_len + kTileK - 1) / kTileK;
+  if (args.causal) n_kv = min(n_kv, (q0 + kTileQ + kTileK - 1) / kTileK);
+  if (skip) n_kv = 0;
   const int colQ = (0 * args.H + h) * HD;
   const int colK = (1 * args.H + h) * HD;
   const int colV = (2 * args.H + h) * HD;
@@ -481,9 +480,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   const int lane = threadIdx.x & 31;
   const int num_pairs = (args.S + 2 * kTileQ - 1) / (2 * kTileQ);
   const int total = args.B * args.H * num_pairs;
-  const bool prefix = args.lengths != nullptr &&
-                      (args.mask_flags == nullptr || __ldg(args.mask_flags) == 0);
-  const bool use_key_mask = args.key_mask != nullptr && !prefix;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -511,6 +507,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const bool prefix = args.lengths != nullptr &&
+                      (args.mask_flags == nullptr || __ldg(args.mask_flags) == 0);
+  const bool use_key_mask = args.key_mask != nullptr && !prefix;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -830,8 +829,7 @@ int launch_attn(const void* qkv, const AttnArgs& args, cudaStream_t stream) {
   const int st = make_tmap_16bit(&tm, 3, qkv, dims, strides, box, args.bf16 != 0);
   if (st != TJB_OK) return st;
   dim3 grid(args.B * args.H, (args.S + kTileQ - 1) / kTileQ);
-  attn_fwd_kernel<HD><<<grid, 192, Cfg::kSmemBytes, stream>>>(tm, args);
-  return launch_status();
+  return launch_kernel(attn_fwd_kernel<HD>, grid, dim3(192), Cfg::kSmemBytes, stream, tm, args);
 }
 
 std::mutex g_pair_attr_mu;
@@ -860,11 +858,10 @@ int launch_attn_pair(const void* qkv, const AttnArgs& args, cudaStream_t stream)
   if (st != TJB_OK) return st;
   const long total = static_cast<long>(args.B) * args.H * ((args.S + 2 * kTileQ - 1) / (2 * kTileQ));
   const int grid = static_cast<int>(total < num_sms() ? total : num_sms());
-  if (args.bf16)
-    attn_pair_kernel<true><<<grid, kPairThreads, PairCfg::kSmemBytes, stream>>>(tm, args);
-  else
-    attn_pair_kernel<false><<<grid, kPairThreads, PairCfg::kSmemBytes, stream>>>(tm, args);
-  return launch_status();
+  return args.bf16 ? launch_kernel(attn_pair_kernel<true>, dim3(grid), dim3(kPairThreads),
+                                PairCfg::kSmemBytes, stream, tm, args)
+                   : launch_kernel(attn_pair_kernel<false>, dim3(grid), dim3(kPairThreads),
+                                PairCfg::kSmemBytes, stream, tm, args);
 }
 
 }  // namespace

@@ -413,6 +413,20 @@ inline int cuda_status(cudaError_t e) {
 
 inline int launch_status() { return cuda_status(cudaGetLastError()); }
 
+// cudaLaunchKernelEx wrapper returning a tjb_status.  (Programmatic
+// dependent launch was measured here: 3% slower on the forward, so plain
+// stream order is used.)
+template <typename... KArgs, typename... Args>
+inline int launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                         cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+}
+
 inline bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }

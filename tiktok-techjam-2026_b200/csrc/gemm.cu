@@ -130,10 +130,6 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_m = args.m_tiles != nullptr ? __ldg(args.m_tiles) : (args.M + kBM - 1) / kBM;
-  const int num_n = (args.N + BN - 1) / BN;
-  const int num_k = (args.K + kBK - 1) / kBK;
-  const int num_tiles = num_m * num_n;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -158,6 +154,10 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const int num_m = args.m_tiles != nullptr ? __ldg(args.m_tiles) : (args.M + kBM - 1) / kBM;
+  const int num_n = (args.N + BN - 1) / BN;
+  const int num_k = (args.K + kBK - 1) / kBK;
+  const int num_tiles = num_m * num_n;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -305,8 +305,8 @@ int launch_gemm(const void* A, const void* B, const GemmArgs& args, int lda, int
   if (st != TJB_OK) return st;
   const int num_tiles = ((args.M + kBM - 1) / kBM) * ((args.N + BN - 1) / BN);
   const int grid = num_tiles < num_sms() ? num_tiles : num_sms();
-  gemm_kernel<BN><<<grid, 192, Cfg::kSmemBytes, stream>>>(tmA, tmB, args);
-  return launch_status();
+  return launch_kernel(gemm_kernel<BN>, dim3(grid), dim3(192), Cfg::kSmemBytes, stream, tmA, tmB,
+                    args);
 }
 
 }  // namespace

@@ -177,18 +177,20 @@ extern "C" int tjb_add_layernorm_tiles(const float* res, const void* delta, floa
   const int64_t tiles = (rows + kTileRows - 1) / kTileRows;
   if (d <= 1024) {
     const int64_t grid = m_tiles ? tiles * (kTileRows / 8) : (rows + 7) / 8;
-    add_layernorm_kernel<32><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
-        res, delta, res_out, out, w, b, rows, d, eps, delta_dtype, out_dtype, row_mask, m_tiles);
+    return launch_kernel(add_layernorm_kernel<32>, dim3(static_cast<unsigned>(grid)),
+                      dim3(kBlock), 0, s, res, delta, res_out, out, w, b, rows, d, eps,
+                      delta_dtype, out_dtype, row_mask, m_tiles);
   } else if (d <= 4096) {
     const int64_t grid = m_tiles ? tiles * (kTileRows / 2) : (rows + 1) / 2;
-    add_layernorm_kernel<128><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
-        res, delta, res_out, out, w, b, rows, d, eps, delta_dtype, out_dtype, row_mask, m_tiles);
+    return launch_kernel(add_layernorm_kernel<128>, dim3(static_cast<unsigned>(grid)),
+                      dim3(kBlock), 0, s, res, delta, res_out, out, w, b, rows, d, eps,
+                      delta_dtype, out_dtype, row_mask, m_tiles);
   } else {
     const int64_t grid = m_tiles ? tiles * kTileRows : rows;
-    add_layernorm_kernel<256><<<static_cast<unsigned>(grid), kBlock, 0, s>>>(
-        res, delta, res_out, out, w, b, rows, d, eps, delta_dtype, out_dtype, row_mask, m_tiles);
+    return launch_kernel(add_layernorm_kernel<256>, dim3(static_cast<unsigned>(grid)),
+                      dim3(kBlock), 0, s, res, delta, res_out, out, w, b, rows, d, eps,
+                      delta_dtype, out_dtype, row_mask, m_tiles);
   }
-  return launch_status();
 }
 
 extern "C" int tjb_add_layernorm(const float* res, const void* delta, float* res_out, void* out,

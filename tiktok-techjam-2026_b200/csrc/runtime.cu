@@ -236,18 +236,16 @@ int tjb_mask_lengths(const uint8_t* mask, int B, int S, int32_t* lengths, int32_
                      tjb_stream_t stream) {
   if (!mask || !lengths || !flags || B <= 0 || S <= 0) return TJB_ERR_INVALID_ARGUMENT;
   if (!tjb::device_ok()) return TJB_ERR_NO_DEVICE;
-  tjb::mask_lengths_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      mask, B, S, lengths, flags);
-  return tjb::launch_status();
+  return tjb::launch_kernel(tjb::mask_lengths_kernel, dim3(1), dim3(1024), 0,
+                         reinterpret_cast<cudaStream_t>(stream), mask, B, S, lengths, flags);
 }
 
 int tjb_row_tiles(const int32_t* lengths, const int32_t* flags, int B, int S, int32_t* tiles,
                   tjb_stream_t stream) {
   if (!tiles || B <= 0 || S <= 0) return TJB_ERR_INVALID_ARGUMENT;
   if (!tjb::device_ok()) return TJB_ERR_NO_DEVICE;
-  tjb::row_tiles_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(lengths, flags,
-                                                                                B, S, tiles);
-  return tjb::launch_status();
+  return tjb::launch_kernel(tjb::row_tiles_kernel, dim3(1), dim3(1024), 0,
+                         reinterpret_cast<cudaStream_t>(stream), lengths, flags, B, S, tiles);
 }
 
 int tjb_selftest_wait(const int32_t* flag, int64_t timeout_ns, tjb_stream_t stream) {

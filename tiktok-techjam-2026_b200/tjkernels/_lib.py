@@ -11,7 +11,11 @@ import ctypes
 import threading
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().with_name("libtjb200.so")
+import os
+
+# The in-tree build; TJB_LIBRARY may name another build of the same ABI.
+LIB_PATH = Path(os.environ.get("TJB_LIBRARY") or
+                Path(__file__).resolve().with_name("libtjb200.so"))
 
 TJB_F32, TJB_F16, TJB_BF16 = 0, 1, 2
 
