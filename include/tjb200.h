@@ -153,6 +153,21 @@ int tjb_ffn_tiles(const void* h, const void* w1, const float* b1, const void* w2
                   int in_dtype, int out_dtype, const int32_t* m_tiles, tjb_stream_t stream);
 
 /*
+ * The feed-forward block as ONE kernel whose [T, F] hidden activations never
+ * leave the SMs: a cluster of d/256 CTAs shares each 128-token tile, each CTA
+ * computing GEMM1 + bias + erf-GELU for a 128-column slice of every hidden
+ * chunk, exchanging the slices through distributed shared memory, and
+ * accumulating its 256 output columns of GEMM2 in tensor memory.
+ * Needs d in {256, 512, 768, 1024} and F % (128 * d / 256) == 0 (else
+ * TJB_ERR_BAD_SHAPE); m_tiles as in tjb_ffn_tiles (nullable).
+ * Replaces the single-kernel fused_ffn of tjkernels/kernels/ffn.py:21-69,
+ * which the reference could only use for d, F <= 256 (ffn.py:103-110).
+ */
+int tjb_ffn_fused(const void* h, const void* w1, const float* b1, const void* w2,
+                  const float* b2, void* out, int T, int d, int F, int in_dtype,
+                  int out_dtype, const int32_t* m_tiles, tjb_stream_t stream);
+
+/*
  * tjb_ffn without any device allocation and without caller scratch: the
  * [T, F] hidden activations live in a 16 MiB device array inside the library
  * (T * F <= TJB_FFN_NOALLOC_MAX_HIDDEN, else TJB_ERR_BAD_SHAPE and nothing is

@@ -289,3 +289,47 @@ def test_gemm_and_layernorm_visit_only_listed_tiles():
             assert torch.equal(new_res[rows], (res0 + delta)[rows])
         else:
             assert torch.equal(new_res[rows], res0[rows])
+
+
+@pytest.mark.parametrize("t,d,f", [(1, 256, 1024), (200, 512, 2048), (1000, 768, 3072),
+                                   (4096, 1024, 4096), (300, 1024, 4096)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_ffn_single_kernel_matches_two_gemm_path(t, d, f, dtype):
+    g = torch.Generator(device=DEV).manual_seed(t + d + f)
+    h = torch.randn(t, d, device=DEV, generator=g).to(dtype)
+    w1 = (torch.randn(f, d, device=DEV, generator=g) / math.sqrt(d)).to(dtype)
+    w2 = (torch.randn(d, f, device=DEV, generator=g) / math.sqrt(f)).to(dtype)
+    b1 = torch.randn(f, device=DEV, generator=g)
+    b2 = torch.randn(d, device=DEV, generator=g)
+    assert K().ffn_fused_supports(d, f)
+    two = K().fused_ffn(h, w1, b1, w2, b2, out_dtype=torch.float32)
+    one = K().ffn_single_kernel(h, w1, b1, w2, b2, out_dtype=torch.float32)
+    # Same products, same k order, hidden rounded to the same 16-bit type.
+    assert (one - two).abs().max().item() < 1e-3
+    hidden = F.gelu(h.double() @ w1.double().T + b1.double(), approximate="none")
+    ref = hidden.to(dtype).double() @ w2.double().T + b2.double()
+    assert (one.double() - ref).abs().max().item() < 2e-2
+
+
+def test_ffn_single_kernel_live_tiles():
+    t, d, f = 1000, 1024, 4096
+    h = torch.randn(t, d, device=DEV).half()
+    w1 = (torch.randn(f, d, device=DEV) / 32).half()
+    w2 = (torch.randn(d, f, device=DEV) / 64).half()
+    b1, b2 = torch.randn(f, device=DEV), torch.randn(d, device=DEV)
+    listed = [1, 3, 7]
+    tiles = torch.tensor([3] + listed + [0] * 5, dtype=torch.int32, device=DEV)
+    full = K().ffn_single_kernel(h, w1, b1, w2, b2, out_dtype=torch.float32)
+    out = K().ffn_single_kernel(h, w1, b1, w2, b2, out_dtype=torch.float32, m_tiles=tiles)
+    for tile in listed:
+        rows = slice(tile * 128, min(tile * 128 + 128, t))
+        assert torch.equal(out[rows], full[rows])
+
+
+def test_ffn_single_kernel_rejects_unsupported():
+    from tjkernels._lib import KernelError
+    h = torch.randn(8, 4096, device=DEV).half()
+    w = torch.randn(16384, 4096, device=DEV).half()
+    with pytest.raises(KernelError):
+        K().ffn_single_kernel(h, w, torch.zeros(16384, device=DEV), w.T.contiguous(),
+                              torch.zeros(4096, device=DEV))

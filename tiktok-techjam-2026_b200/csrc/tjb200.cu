@@ -5,3 +5,4 @@
 #include "gemm.cu"
 #include "attention.cu"
 #include "ffn.cu"
+#include "ffn_fused.cu"

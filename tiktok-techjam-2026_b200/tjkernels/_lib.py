@@ -40,6 +40,8 @@ SIGNATURES = {
                          _c_int, _p]),
     "tjb_ffn_tiles": (_c_int, [_p, _p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int,
                                _c_int, _p, _p]),
+    "tjb_ffn_fused": (_c_int, [_p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int,
+                               _p, _p]),
     "tjb_row_tiles": (_c_int, [_p, _p, _c_int, _c_int, _p, _p]),
     "tjb_ffn_noalloc": (_c_int, [_p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int,
                                  _c_int, _p]),

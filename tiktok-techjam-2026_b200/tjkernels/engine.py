@@ -161,8 +161,10 @@ class Engine:
                 res, attn_out, lw.ln2_w, lw.ln2_b, lw.ln2_eps, out_dtype=plan.compute_dtype,
                 residual_out=res if own_res else None, m_tiles=tiles)
             own_res = True
-            pending = K.fused_ffn(h2, lw.w1, lw.b1, lw.w2, lw.b2, out_dtype=plan.delta_dtype,
-                                  m_tiles=tiles)
+            ffn = K.ffn_single_kernel if (plan.ffn_single_kernel and
+                                          K.ffn_fused_supports(d, self.ffn_dim)) else K.fused_ffn
+            pending = ffn(h2, lw.w1, lw.b1, lw.w2, lw.b2, out_dtype=plan.delta_dtype,
+                          m_tiles=tiles)
 
         fw, fb, feps = self.final_ln
         _, out = K.fused_add_layernorm(res, pending, fw, fb, feps, out_dtype=self.dtype,

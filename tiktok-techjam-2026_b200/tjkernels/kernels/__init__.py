@@ -137,6 +137,29 @@ def fused_ffn(h: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor, w2: torch.Ten
     return out
 
 
+def ffn_fused_supports(d_model: int, ffn_dim: int) -> bool:
+    """Shapes the single-kernel FFN (hidden kept on chip) handles."""
+    c = d_model // 256
+    return d_model % 256 == 0 and 1 <= c <= 4 and ffn_dim % (128 * c) == 0
+
+
+def ffn_single_kernel(h: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor, w2: torch.Tensor,
+                      b2: torch.Tensor, out_dtype: Optional[torch.dtype] = None,
+                      m_tiles: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Same result as ``fused_ffn`` from one kernel whose [T, F] hidden tile
+    never reaches HBM (``tjb_ffn_fused``); raises for unsupported shapes."""
+    _need_cuda(h, w1, b1, w2, b2)
+    t, d = h.shape
+    f = w1.shape[0]
+    out_dtype = out_dtype or h.dtype
+    out = torch.empty((t, d), dtype=out_dtype, device=h.device)
+    status = _lib.lib().tjb_ffn_fused(
+        _ptr(h), _ptr(w1), _ptr(b1), _ptr(w2), _ptr(b2), _ptr(out), t, d, f,
+        _code(h.dtype), _code(out_dtype), _ptr(m_tiles), _stream(h.device))
+    _lib.check(status, "tjb_ffn_fused")
+    return out
+
+
 def flash_supports(head_dim: int, causal: bool = True) -> bool:
     return head_dim in (64, 128)
 
@@ -199,5 +222,6 @@ def device_status(clear: bool = False) -> int:
 
 __all__ = [
     "ACT_NONE", "ACT_GELU", "fused_add_layernorm", "layernorm", "gemm_bias", "fused_ffn",
+    "ffn_single_kernel", "ffn_fused_supports",
     "flash_attention", "flash_supports", "mask_lengths", "row_tiles", "device_status",
 ]

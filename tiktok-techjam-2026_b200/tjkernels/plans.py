@@ -48,6 +48,12 @@ class Plan:
     # Skip the GEMM / LayerNorm work of 128-row tiles that hold only padding
     # (prefix masks); padded rows still come out exactly zero.
     skip_padding: bool = True
+    # Run the FFN as one kernel whose hidden tile never reaches HBM
+    # (tjb_ffn_fused, d_model <= 1024) instead of two GEMM launches through a
+    # hidden scratch.  Off by default: measured 2.2x slower on B200 at
+    # d_model 1024 (its shared-memory hidden chunk leaves room for only a
+    # 3-stage operand ring).
+    ffn_single_kernel: bool = False
     label: str = "default"
 
     def to_json(self) -> Dict[str, object]:
@@ -57,6 +63,7 @@ class Plan:
             "delta_dtype": _DTYPE_NAMES[self.delta_dtype],
             "cuda_graph": self.cuda_graph,
             "skip_padding": self.skip_padding,
+            "ffn_single_kernel": self.ffn_single_kernel,
             "label": self.label,
         }
 
@@ -133,6 +140,8 @@ def select_plan(batch: int, seq: int, d_model: int, heads: int, ffn_dim: int, la
     forced = os.environ.get("TJ_COMPUTE_DTYPE")
     if forced in ("float16", "bfloat16"):
         plan = replace(plan, compute_dtype=_DTYPES[forced])
+    if os.environ.get("TJ_FFN_SINGLE_KERNEL") == "1":
+        plan = replace(plan, ffn_single_kernel=True)
     if os.environ.get("TJ_NO_SKIP") == "1":
         plan = replace(plan, skip_padding=False)
     forced = os.environ.get("TJ_DELTA_DTYPE")
