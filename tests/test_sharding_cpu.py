@@ -79,3 +79,35 @@ def test_two_rank_batch_shard_equals_full_forward(tmp_path):
     x, mask = generate_case(cfg, 7, 0.5)
     full = oracle_forward(model, x, mask)
     assert (gathered - full).abs().max().item() < 1e-5
+
+
+def _leaver_main(rank, world, port, out_path):
+    """Rank 1 leaves between steps without joining the barrier; rank 0 must
+    get an error from the collective instead of waiting forever."""
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    dist.barrier()  # one healthy step
+    if rank == 1:
+        os._exit(0)  # dies with no collective in flight
+    t0 = time.time()
+    try:
+        dist.barrier()
+        outcome = "completed"
+    except Exception as exc:  # gloo reports the lost peer or the timeout
+        outcome = f"raised after {time.time() - t0:.1f}s: {type(exc).__name__}"
+    with open(out_path, "w") as f:
+        f.write(outcome)
+    os._exit(0)
+
+
+def test_survivor_raises_when_a_rank_dies(tmp_path):
+    out_path = str(tmp_path / "outcome.txt")
+    mp.start_processes(_leaver_main, args=(2, _free_port(), out_path), nprocs=2, join=True,
+                       start_method="spawn")
+    with open(out_path) as f:
+        outcome = f.read()
+    assert outcome.startswith("raised"), outcome
+    assert float(outcome.split()[2].rstrip("s:")) < 30.0
