@@ -713,16 +713,17 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         }
         const float mb = m_ref == -INFINITY ? 0.f : m_ref * sl2;
         // Exponentials into registers (64 packed pairs) before P is touched.
-        // Alternate pairs go to the MUFU unit and to a polynomial on the FMA
-        // pipe, which together issue twice the exponentials the MUFU alone
-        // can.  Row sums in fp32 (packed adds, two chains).
+        // One pair in four goes to a polynomial on the FMA pipe, the rest to
+        // the MUFU unit (measured at B4 S4096: 1/4 -> 468 TFLOP/s, 1/2 -> 448,
+        // 3/4 -> 380, none -> 460; the MUFU is no longer the limit once P
+        // lives in tensor memory).  Row sums in fp32 (packed adds, two chains).
         uint32_t e[kTileK / 2];
         float sa0 = 0.f, sa1 = 0.f, sb0 = 0.f, sb1 = 0.f;
 #pragma unroll
         for (int c = 0; c < kTileK / 2; ++c) {
           float x0, x1, p0, p1;
           ffma2(x0, x1, __uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1]), sl2, -mb);
-          if (c & 1) {
+          if ((c & 3) == 0) {
             exp2_poly2(p0, p1, x0, x1);
             add2v(sb0, sb1, p0, p1);
           } else {
