@@ -132,7 +132,8 @@ def attn_reference(qkv, causal, lengths=None, key_mask=None):
 
 
 ATTN_CASES = [(1, 1, 1, 64), (2, 37, 2, 64), (2, 128, 4, 64), (1, 200, 2, 128),
-              (2, 256, 2, 64), (1, 1000, 2, 64), (1, 513, 1, 128), (2, 2048, 2, 64)]
+              (2, 256, 2, 64), (1, 1000, 2, 64), (1, 513, 1, 128), (2, 2048, 2, 64),
+              (1, 1, 1, 128), (3, 300, 4, 128), (2, 2048, 2, 128)]
 
 
 @pytest.mark.parametrize("b,s,h,hd", ATTN_CASES)
@@ -167,8 +168,9 @@ def test_flash_prefix_lengths(causal, hd):
     assert torch.isfinite(out).all()
 
 
-def test_flash_general_key_mask():
-    b, s, h, hd = 2, 300, 2, 64
+@pytest.mark.parametrize("hd", [64, 128])
+def test_flash_general_key_mask(hd):
+    b, s, h = 2, 300, 2
     qkv = torch.randn(b, s, 3, h, hd, device=DEV).bfloat16()
     key_mask = (torch.rand(b, s, device=DEV) > 0.3)
     key_mask[:, 0] = True

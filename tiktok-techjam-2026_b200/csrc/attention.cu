@@ -1,24 +1,28 @@
 // attention.cu -- causal / full multi-head attention forward on tcgen05.
 //
-// One CTA computes one 128-row query tile of one (batch, head) pair straight
-// from the packed QKV projection output [B, S, 3, H, hd] (read in place by
-// TMA through a 3-D tensor map over [B][S][3*H*hd]; rows past S zero-fill)
-// and writes its context rows into out[B*S, H*hd] at column h*hd.
+// Reads Q, K and V straight from the packed QKV projection output
+// [B, S, 3, H, hd] (TMA through a 3-D tensor map over [B][S][3*H*hd]; rows
+// past S zero-fill) and writes context rows into out[B*S, H*hd] at column
+// h*hd.  head_dim 64 or 128.
 //
-// Roles (192 threads):
-//   warp 0      TMA producer: Q once, then (K_j, V_j) 128-row tiles into a
-//               kStages ring.
-//   warp 1      TMEM owner; one lane issues S_j = Q K_j^T (M=N=128, K=hd)
-//               into one of two TMEM score buffers, and O += P_j V_j (M=128,
-//               N=hd, K=128; V read MN-major) into the TMEM output
-//               accumulator.  QK of tile j+1 is issued before PV of tile j,
-//               so the tensor core works while the softmax runs.
-//   warps 2..5  softmax: thread r owns query row r; reads its score row from
-//               TMEM, applies causal / length / key masks, keeps the running
-//               max and sum in fp32 (exp2 with log2(e) folded into the
-//               scale), rescales O in TMEM when the max grows, writes P as
-//               16-bit values into a 128-byte-swizzled shared-memory tile for
-//               the PV MMA, and finally writes O / l.
+// One persistent kernel, one CTA per SM.  A CTA walks work items (batch*head,
+// pair of consecutive 128-row query tiles), heaviest causal rows first.  The
+// two query tiles are owned by two softmax warp groups that run against one
+// MMA issuer, so while group 0 computes its softmax the tensor core works on
+// group 1's products and vice versa; each K/V tile is loaded once for both.
+//   warp 0        TMA producer: the item's Q pair (double-buffered at
+//                 head_dim 64, so it lands while the previous item runs),
+//                 then (K_j, V_j) 128-row tiles into a stage ring
+//   warp 1        TMEM owner + MMA issuer (one lane):
+//                   S_g = Q_g K_j^T  (M=N=128, K=hd) into TMEM
+//                   O_g += P_g V_j   (M=128, N=hd, K=128; V read MN-major,
+//                                     P read from TMEM as the A operand)
+//   warps 2-5     softmax group 0 (query rows q0 .. q0+127)
+//   warps 6-9     softmax group 1 (query rows q0+128 .. q0+255)
+// Softmax thread r owns query row r: it reads its score row from TMEM,
+// applies causal / length / key masks, keeps the running max and sum in fp32
+// (exp2 with log2(e) folded into the scale), rescales O in TMEM when the max
+// grows, writes P as 16-bit pairs back into TMEM and finally writes O / l.
 // Key tiles above the diagonal are never loaded; only tiles that cross the
 // diagonal or a length boundary are masked.  With a prefix padding mask,
 // query tiles wholly past the sequence's valid length are skipped (their
@@ -33,18 +37,6 @@ namespace {
 constexpr int kTileQ = 128;
 constexpr int kTileK = 128;
 constexpr uint32_t kSub = 128 * 64 * 2;  // one 128-row x 64-column 16-bit sub-tile
-
-template <int HD>
-struct AttnCfg {
-  static constexpr int kSubs = HD / 64;
-  static constexpr int kStages = HD == 64 ? 3 : 2;
-  static constexpr uint32_t kQBytes = kSubs * kSub;
-  static constexpr uint32_t kKVBytes = 2 * kSubs * kSub;  // K tile + V tile
-  static constexpr uint32_t kPBytes = 2 * kSub;            // 128 x 128 16-bit
-  static constexpr uint32_t kSmemBytes = 1024 + kQBytes + kStages * kKVBytes + 2 * kPBytes + 256;
-  static constexpr uint32_t kTmemCols = 512;  // S0 [0,128), S1 [128,256), O [256, 256+HD)
-  static constexpr uint32_t kOCol = 256;
-};
 
 struct AttnArgs {
   void* out;
@@ -64,362 +56,40 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-template <int HD>
-__global__ void __launch_bounds__(192, 1)
-    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, const AttnArgs args) {
-  using Cfg = AttnCfg<HD>;
-  constexpr int kStages = Cfg::kStages;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sKV = sQ + Cfg::kQBytes;
-  uint8_t* sP = sKV + kStages * Cfg::kKVBytes;
-  uint64_t* q_full = reinterpret_cast<uint64_t*>(sP + 2 * Cfg::kPBytes);
-  uint64_t* kv_full = q_full + 1;
-  uint64_t* kv_empty = kv_full + kStages;
-  uint64_t* s_full = kv_empty + kStages;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* pv_done = p_full + 2;
-  uint64_t* drain = pv_done + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int bh = blockIdx.x;
-  const int b = bh / args.H;
-  const int h = bh - b * args.H;
-  const int num_q_tiles = (args.S + kTileQ - 1) / kTileQ;
-  const int q_tile = num_q_tiles - 1 - static_cast<int>(blockIdx.y);  // longest rows first
-  const int q0 = q_tile * kTileQ;
-
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
-      mbar_init(&pv_done[i], 1);
-    }
-    mbar_init(drain, 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-    prefetch_tmap(&tm);
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-  // Visible key range and skipping decided from the padding description.
-  const bool prefix = args.lengths != nullptr &&
-                      (args.mask_flags == nullptr || __ldg(args.mask_flags) == 0);
-  const bool use_key_mask = args.key_mask != nullptr && !prefix;
-  int kv_len = args.S;
-  bool skip = false;
-  if (prefix) {
-    const int len = __ldg(args.lengths + b);
-    kv_len = min(max(len, 0), args.S);
-    skip = q0 >= kv_len;
-  }
-  int n_kv = (kv_len + kTileK - 1) / kTileK;
-  if (args.causal) n_kv = min(n_kv, (q0 + kTileQ + kTileK - 1) / kTileK);
-  if (skip) n_kv = 0;
-  const int colQ = (0 * args.H + h) * HD;
-  const int colK = (1 * args.H + h) * HD;
-  const int colV = (2 * args.H + h) * HD;
-
-  if (warp == 0) {
-    if (lane == 0 && n_kv > 0) {
-      // ------------------------------------------------------------ producer
-      mbar_arrive_expect_tx(q_full, Cfg::kQBytes);
-#pragma unroll
-      for (int sub = 0; sub < Cfg::kSubs; ++sub)
-        tma_load_3d(sQ + sub * kSub, &tm, q_full, colQ + sub * 64, q0, b);
-      int stage = 0;
-      uint32_t phase = 0, issued = 0, issued_parity = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        if (!mbar_wait(&kv_empty[stage], phase ^ 1, abort_flag)) break;
-        uint8_t* sK = sKV + stage * Cfg::kKVBytes;
-        uint8_t* sV = sK + Cfg::kSubs * kSub;
-        mbar_arrive_expect_tx(&kv_full[stage], Cfg::kKVBytes);
-#pragma unroll
-        for (int sub = 0; sub < Cfg::kSubs; ++sub) {
-          tma_load_3d(sK + sub * kSub, &tm, &kv_full[stage], colK + sub * 64, j * kTileK, b);
-          tma_load_3d(sV + sub * kSub, &tm, &kv_full[stage], colV + sub * 64, j * kTileK, b);
-        }
-        issued |= 1u << stage;
-        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1;
-        }
-      }
-      mbar_wait_drain(q_full, 0);
-      for (int s = 0; s < kStages; ++s)
-        if ((issued >> s) & 1u) mbar_wait_drain(&kv_full[s], (issued_parity >> s) & 1u);
-    }
-  } else if (warp == 1) {
-    if (lane == 0 && n_kv > 0) {
-      // ---------------------------------------------------------- MMA issuer
-      const uint32_t q_addr = smem_u32(sQ);
-      const uint32_t p_addr = smem_u32(sP);
-      bool ok = mbar_wait(q_full, 0, abort_flag);
-      int stage = 0;
-      uint32_t phase = 0;
-      int prev_stage = 0;
-      for (int j = 0; j <= n_kv && ok; ++j) {
-        if (j < n_kv) {
-          if (!mbar_wait(&kv_full[stage], phase, abort_flag)) break;
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(sKV + stage * Cfg::kKVBytes);
-          const uint32_t d_s = tmem_base + static_cast<uint32_t>((j & 1) * kTileK);
-#pragma unroll
-          for (int k = 0; k < HD / 16; ++k) {
-            const uint32_t off = (k >> 2) * kSub + (k & 3) * 32;
-            umma_ss(d_s, sdesc_sw128(q_addr + off, 16, 1024), sdesc_sw128(k_addr + off, 16, 1024),
-                    args.idesc_qk, k > 0 ? 1u : 0u);
-          }
-          umma_commit(&s_full[j & 1]);
-        }
-        if (j >= 1) {
-          const int jp = j - 1;
-          if (!mbar_wait(&p_full[jp & 1], (jp >> 1) & 1, abort_flag)) break;
-          tc_fence_after();
-          const uint32_t v_addr =
-              smem_u32(sKV + prev_stage * Cfg::kKVBytes) + Cfg::kSubs * kSub;
-          const uint32_t pa = p_addr + (jp & 1) * Cfg::kPBytes;
-#pragma unroll
-          for (int k = 0; k < kTileK / 16; ++k) {
-            const uint32_t a_off = (k >> 2) * kSub + (k & 3) * 32;
-            umma_ss(tmem_base + Cfg::kOCol, sdesc_sw128(pa + a_off, 16, 1024),
-                    sdesc_sw128(v_addr + k * 2048, kSub, 1024), args.idesc_pv,
-                    (jp > 0 || k > 0) ? 1u : 0u);
-          }
-          umma_commit(&pv_done[jp & 1]);
-          umma_commit(&kv_empty[prev_stage]);
-        }
-        prev_stage = stage;
-        if (j < n_kv && ++stage == kStages) {
-          stage = 0;
-          phase ^= 1;
-        }
-      }
-      umma_commit(drain);
-      mbar_wait_drain(drain, 0);
-    }
-  } else {
-    // ---------------------------------------------------------------- softmax
-    const int quad = warp & 3;
-    const int r = quad * 32 + lane;
-    const int qi = q0 + r;
-    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
-    const int64_t out_row = static_cast<int64_t>(b) * args.S + qi;
-    uint16_t* out_ptr = static_cast<uint16_t*>(args.out) + out_row * args.ldo + h * HD;
-    if (n_kv == 0) {
-      if (qi < args.S) {
-#pragma unroll
-        for (int c = 0; c < HD / 8; ++c)
-          reinterpret_cast<uint4*>(out_ptr)[c] = make_uint4(0u, 0u, 0u, 0u);
-      }
-    } else {
-      const float sl2 = args.scale_log2;
-      float m_i = -INFINITY;  // running max of raw scores
-      float l_i = 0.f;
-      bool ok = true;
-      for (int j = 0; j < n_kv; ++j) {
-        bool w_ok = mbar_wait(&s_full[j & 1], (j >> 1) & 1, abort_flag);
-        if (!__all_sync(0xffffffffu, w_ok)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        float s[kTileK];
-        {
-          uint32_t raw[32];
-#pragma unroll
-          for (int c = 0; c < kTileK / 32; ++c) {
-            tmem_ld32(lane_base + static_cast<uint32_t>((j & 1) * kTileK + c * 32), raw);
-            tmem_ld_wait(raw);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(raw[i]);
-          }
-        }
-        const int kv0 = j * kTileK;
-        const bool need_mask = (args.causal && kv0 + kTileK - 1 > q0) || (kv0 + kTileK > kv_len) ||
-                               use_key_mask;
-        if (need_mask) {
-          const uint8_t* km =
-              use_key_mask ? args.key_mask + static_cast<int64_t>(b) * args.S : nullptr;
-#pragma unroll
-          for (int c = 0; c < kTileK; ++c) {
-            const int kj = kv0 + c;
-            bool masked = kj >= kv_len || (args.causal && kj > qi);
-            if (km != nullptr && kj < args.S && km[kj] == 0) masked = true;
-            if (masked) s[c] = -INFINITY;
-          }
-        }
-        float mx = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < kTileK; ++c) mx = fmaxf(mx, s[c]);
-        const float m_new = fmaxf(m_i, mx);
-        // All-masked rows keep m = -inf; use 0 as the exponent base so every
-        // p is exactly 0 instead of NaN.
-        const float m_use = m_new == -INFINITY ? 0.f : m_new;
-        const float alpha = fast_exp2((m_i - m_use) * sl2);  // 0 on the first tile
-        const bool grow = m_new > m_i;
-        // Rescale O in TMEM once the previous PV has landed.
-        if (j > 0 && __any_sync(0xffffffffu, grow)) {
-          const int jp = j - 1;
-          w_ok = mbar_wait(&pv_done[jp & 1], (jp >> 1) & 1, abort_flag);
-          if (!__all_sync(0xffffffffu, w_ok)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const float a = grow ? alpha : 1.f;
-#pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
-            uint32_t o[32];
-            const uint32_t ta = lane_base + Cfg::kOCol + c * 32;
-            tmem_ld32(ta, o);
-            tmem_ld_wait(o);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * a);
-            tmem_st32(ta, o);
-          }
-          tmem_st_wait();
-        }
-        if (grow) {
-          l_i *= alpha;
-          m_i = m_new;
-        }
-        const float mb = m_use * sl2;
-        float rowsum = 0.f;
-#pragma unroll
-        for (int c = 0; c < kTileK; ++c) {
-          s[c] = fast_exp2(fmaf(s[c], sl2, -mb));
-          rowsum += s[c];
-        }
-        l_i += rowsum;
-        // P buffer (j & 1) is free once PV of tile j-2 has completed.
-        if (j >= 2) {
-          const int jq = j - 2;
-          w_ok = mbar_wait(&pv_done[jq & 1], (jq >> 1) & 1, abort_flag);
-          if (!__all_sync(0xffffffffu, w_ok)) {
-            ok = false;
-            break;
-          }
-        }
-        uint8_t* prow = sP + (j & 1) * Cfg::kPBytes + r * 128;
-#pragma unroll
-        for (int cc = 0; cc < kTileK / 8; ++cc) {
-          const int sub = cc >> 3, c8 = cc & 7;
-          uint4 v;
-          if (args.bf16) {
-            v.x = Pack2<__nv_bfloat16>::pack(s[cc * 8 + 0], s[cc * 8 + 1]);
-            v.y = Pack2<__nv_bfloat16>::pack(s[cc * 8 + 2], s[cc * 8 + 3]);
-            v.z = Pack2<__nv_bfloat16>::pack(s[cc * 8 + 4], s[cc * 8 + 5]);
-            v.w = Pack2<__nv_bfloat16>::pack(s[cc * 8 + 6], s[cc * 8 + 7]);
-          } else {
-            v.x = Pack2<__half>::pack(s[cc * 8 + 0], s[cc * 8 + 1]);
-            v.y = Pack2<__half>::pack(s[cc * 8 + 2], s[cc * 8 + 3]);
-            v.z = Pack2<__half>::pack(s[cc * 8 + 4], s[cc * 8 + 5]);
-            v.w = Pack2<__half>::pack(s[cc * 8 + 6], s[cc * 8 + 7]);
-          }
-          *reinterpret_cast<uint4*>(prow + sub * kSub + ((c8 ^ (r & 7)) << 4)) = v;
-        }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[j & 1]);
-      }
-      if (ok) {
-        const int jl = n_kv - 1;
-        const bool w_ok = mbar_wait(&pv_done[jl & 1], (jl >> 1) & 1, abort_flag);
-        if (__all_sync(0xffffffffu, w_ok)) {
-          tc_fence_after();
-          const float inv_l = l_i > 0.f ? 1.f / l_i : 0.f;
-#pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(lane_base + Cfg::kOCol + c * 32, o);
-            tmem_ld_wait(o);
-            if (qi < args.S) {
-              uint32_t p[16];
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const float x0 = __uint_as_float(o[2 * i]) * inv_l;
-                const float x1 = __uint_as_float(o[2 * i + 1]) * inv_l;
-                p[i] = args.bf16 ? Pack2<__nv_bfloat16>::pack(x0, x1) : Pack2<__half>::pack(x0, x1);
-              }
-              uint4* dst = reinterpret_cast<uint4*>(out_ptr + c * 32);
-#pragma unroll
-              for (int i = 0; i < 4; ++i)
-                dst[i] = make_uint4(p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
-            }
-          }
-        }
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    __syncwarp();
-    tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::kTmemCols);
-  }
-}
-
-// ===========================================================================
-// Paired-tile persistent kernel (head_dim 64).
-//
-// Each CTA (one per SM) walks work items (batch*head, pair of consecutive
-// 128-row query tiles), heaviest causal rows first.  The two query tiles are
-// owned by two softmax warp groups that run against one MMA issuer, so while
-// group 0 computes its softmax the tensor core works on group 1's products
-// and vice versa; K/V tiles are loaded once for both groups.
-//   warp 0        TMA producer: the next item's Q pair (double-buffered, so
-//                 it lands while the current item runs), then K/V tiles into
-//                 a 4-stage ring
-//   warp 1        TMEM owner + MMA issuer:
-//                   S_g = Q_g K_j^T  (g = 0, 1), as soon as group g has
-//                   pulled its previous scores out of TMEM;
-//                   O_g += P_g V_j   once group g has written P_g.
-//   warps 2-5     softmax group 0 (query rows q0 .. q0+127)
-//   warps 6-9     softmax group 1 (query rows q0+128 .. q0+255)
 // Ten warps put three on two of the SM's four sub-partitions, which caps a
 // thread at 168 registers; the softmax (a 128-score row in registers) fits.
-// P lives in tensor memory (one buffer per group; the PV MMA reads it as its
-// A operand), so it never round-trips through shared memory.  Each group's
-// exponentials are computed into registers before P is overwritten, so the
-// wait for the previous PV overlaps the math.
+// Each group's exponentials are computed into registers before P is
+// written, so the wait for the tensor core overlaps the math.
 // O is rescaled lazily: only when a row's max grows by more than 2^8 (P stays
 // below 256 in 16-bit, every sum stays in fp32 range); O / l is exact for any
 // choice of the reference max.
 constexpr int kPairThreads = 320;
 constexpr float kRescaleLog2 = 8.0f;
 
+template <int HD_>
 struct PairCfg {
-  static constexpr int HD = 64;
-  static constexpr int kStages = 4;
-  static constexpr uint32_t kQBytes = kSub;       // one 128 x 64 tile per group
-  static constexpr uint32_t kKVBytes = 2 * kSub;  // K tile + V tile
-  static constexpr uint32_t kSmemBytes = 1024 + 4 * kQBytes + kStages * kKVBytes + 256;
-  // TMEM columns: S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384)
-  // P0 [384,448) P1 [448,512) (P: 128 x 128 16-bit, two values per column).
+  static constexpr int HD = HD_;
+  static constexpr int kSubs = HD / 64;
+  // head_dim 64: S, O and a separate P per group fit the 512 TMEM columns, so
+  // scores are released as soon as they are in registers.  head_dim 128: S
+  // and O fill TMEM, so P is written over its own group's score columns and
+  // the MMA issues PV of tile j-1 before QK of tile j (the tensor pipe runs
+  // in order, so the next scores never overwrite an unread P).
+  static constexpr bool kAlias = HD > 64;
+  static constexpr int kQSlots = HD == 64 ? 2 : 1;
+  static constexpr int kStages = HD == 64 ? 4 : 2;
+  static constexpr uint32_t kQBytes = kSubs * kSub;       // one 128 x HD tile per group
+  static constexpr uint32_t kKVBytes = 2 * kSubs * kSub;  // K tile + V tile
+  static constexpr uint32_t kSmemBytes =
+      1024 + 2 * kQSlots * kQBytes + kStages * kKVBytes + 256;
+  // TMEM columns, head_dim 64: S0 [0,128) S1 [128,256) O0 [256,320)
+  // O1 [320,384) P0 [384,448) P1 [448,512); head_dim 128: S0/P0 [0,128)
+  // S1/P1 [128,256) O0 [256,384) O1 [384,512).  P: 128 x 128 16-bit, two
+  // values per column.
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kOCol = 256;
-  static constexpr uint32_t kPCol = 384;
+  static constexpr uint32_t kPCol = kAlias ? 0 : 384;
+  static constexpr uint32_t kPStride = kAlias ? 128 : 64;
 };
 
 struct PairItem {
@@ -453,17 +123,18 @@ __device__ __forceinline__ PairItem decode_pair(int w, const AttnArgs& a, int nu
   return it;
 }
 
-template <bool kBF16>
+template <int HD, bool kBF16>
 __global__ void __launch_bounds__(kPairThreads, 1)
     attn_pair_kernel(const __grid_constant__ CUtensorMap tm, const AttnArgs args) {
-  using Cfg = PairCfg;
-  constexpr int HD = Cfg::HD;
+  using Cfg = PairCfg<HD>;
   constexpr int kStages = Cfg::kStages;
+  constexpr int kSubs = Cfg::kSubs;
+  constexpr uint32_t kQSlots = Cfg::kQSlots;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sQ = smem;                                 // [slot][group][kQBytes]
-  uint8_t* sKV = sQ + 4 * Cfg::kQBytes;               // [kStages][K | V]
+  uint8_t* sKV = sQ + 2 * kQSlots * Cfg::kQBytes;     // [kStages][K | V]
   uint64_t* q_full = reinterpret_cast<uint64_t*>(sKV + kStages * Cfg::kKVBytes);  // [slot]
   uint64_t* q_empty = q_full + 2;                                          // [slot]
   uint64_t* kv_full = q_empty + 2;
@@ -521,17 +192,19 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const PairItem it = decode_pair(w, args, num_pairs, prefix);
         const int n = max(it.n_kv[0], it.n_kv[1]);
         if (n == 0) continue;
-        const uint32_t slot = n_items & 1;
-        // The slot was last used by item n_items - 2.
-        if (n_items >= 2 && !mbar_wait(&q_empty[slot], ((n_items - 2) >> 1) & 1, abort_flag))
+        const uint32_t slot = n_items % kQSlots;
+        // The slot was last used by item n_items - kQSlots.
+        if (n_items >= kQSlots &&
+            !mbar_wait(&q_empty[slot], ((n_items - kQSlots) / kQSlots) & 1, abort_flag))
           break;
         const int colQ = it.h * HD;
         const int ntiles = (it.n_kv[0] > 0) + (it.n_kv[1] > 0);
         mbar_arrive_expect_tx(&q_full[slot], ntiles * Cfg::kQBytes);
         for (int g = 0; g < 2; ++g)
           if (it.n_kv[g] > 0)
-            tma_load_3d(sQ + (slot * 2 + g) * Cfg::kQBytes, &tm, &q_full[slot], colQ,
-                        it.q0 + g * kTileQ, it.b);
+            for (int sub = 0; sub < kSubs; ++sub)
+              tma_load_3d(sQ + (slot * 2 + g) * Cfg::kQBytes + sub * kSub, &tm, &q_full[slot],
+                          colQ + sub * 64, it.q0 + g * kTileQ, it.b);
         ++n_items;
         const int colK = (args.H + it.h) * HD;
         const int colV = (2 * args.H + it.h) * HD;
@@ -542,8 +215,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           }
           uint8_t* sK = sKV + stage * Cfg::kKVBytes;
           mbar_arrive_expect_tx(&kv_full[stage], Cfg::kKVBytes);
-          tma_load_3d(sK, &tm, &kv_full[stage], colK, j * kTileK, it.b);
-          tma_load_3d(sK + kSub, &tm, &kv_full[stage], colV, j * kTileK, it.b);
+          for (int sub = 0; sub < kSubs; ++sub) {
+            tma_load_3d(sK + sub * kSub, &tm, &kv_full[stage], colK + sub * 64, j * kTileK, it.b);
+            tma_load_3d(sK + (kSubs + sub) * kSub, &tm, &kv_full[stage], colV + sub * 64,
+                        j * kTileK, it.b);
+          }
           issued |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == kStages) {
@@ -552,8 +228,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           }
         }
       }
-      for (uint32_t k = n_items >= 2 ? n_items - 2 : 0; k < n_items; ++k)
-        mbar_wait_drain(&q_full[k & 1], (k >> 1) & 1);
+      for (uint32_t k = n_items >= kQSlots ? n_items - kQSlots : 0; k < n_items; ++k)
+        mbar_wait_drain(&q_full[k % kQSlots], (k / kQSlots) & 1);
       for (int s = 0; s < kStages; ++s)
         if ((issued >> s) & 1u) mbar_wait_drain(&kv_full[s], (issued_parity >> s) & 1u);
     }
@@ -569,59 +245,77 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const PairItem it = decode_pair(w, args, num_pairs, prefix);
         const int n = max(it.n_kv[0], it.n_kv[1]);
         if (n == 0) continue;
-        const uint32_t slot = n_items & 1;
-        if (!mbar_wait(&q_full[slot], (n_items >> 1) & 1, abort_flag)) break;
+        const uint32_t slot = n_items % kQSlots;
+        if (!mbar_wait(&q_full[slot], (n_items / kQSlots) & 1, abort_flag)) break;
         ++n_items;
         const uint32_t q_addr = q_base + slot * 2 * Cfg::kQBytes;
         for (int j = 0; j <= n && ok; ++j) {
-          if (j < n) {
-            if (!mbar_wait(&kv_full[stage], phase, abort_flag)) {
-              ok = false;
-              break;
+          const uint32_t k_addr = smem_u32(sKV + stage * Cfg::kKVBytes);
+          const uint32_t v_addr = smem_u32(sKV + prev_stage * Cfg::kKVBytes) + kSubs * kSub;
+          bool k_ready = j >= n;
+          // S_g = Q_g K_j^T (HD/16 K-steps over kSubs 64-column sub-tiles).
+          auto issue_qk = [&](int g) {
+            if (!k_ready) {
+              if (!mbar_wait(&kv_full[stage], phase, abort_flag)) return false;
+              tc_fence_after();
+              k_ready = true;
             }
+            const uint32_t qa = q_addr + g * Cfg::kQBytes;
+            const uint32_t d_s = tmem_base + static_cast<uint32_t>(g * kTileK);
+#pragma unroll
+            for (int k = 0; k < HD / 16; ++k) {
+              const uint32_t off = (k >> 2) * kSub + (k & 3) * 32;
+              umma_ss(d_s, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(k_addr + off, 16, 1024),
+                      args.idesc_qk, k > 0 ? 1u : 0u);
+            }
+            umma_commit(&s_full[g]);
+            ++sc[g];
+            return true;
+          };
+          // O_g += P_g V_{j-1}, P_g read from tensor memory.
+          auto issue_pv = [&](int g, int jp) {
+            if (!mbar_wait(&p_full[g], pvc[g] & 1, abort_flag)) return false;
             tc_fence_after();
-            const uint32_t k_addr = smem_u32(sKV + stage * Cfg::kKVBytes);
-            for (int g = 0; g < 2 && ok; ++g) {
-              if (j >= it.n_kv[g]) continue;
+            const uint32_t pa = tmem_base + Cfg::kPCol + g * Cfg::kPStride;
+            const uint32_t d_o = tmem_base + Cfg::kOCol + g * HD;
+#pragma unroll
+            for (int k = 0; k < kTileK / 16; ++k)
+              umma_ts(d_o, pa + k * 8, sdesc_sw128(v_addr + k * 2048, kSub, 1024),
+                      args.idesc_pv, (jp > 0 || k > 0) ? 1u : 0u);
+            umma_commit(&pv_done[g]);
+            ++pvc[g];
+            return true;
+          };
+          if constexpr (Cfg::kAlias) {
+            // Per group: PV of tile j-1 (reads P out of the score columns),
+            // then QK of tile j into the same columns.  The stage of tile j-1
+            // is released once both PVs are issued.
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+              if (ok && j >= 1 && j - 1 < it.n_kv[g]) ok = issue_pv(g, j - 1);
+              if (ok && g == 1 && j >= 1) umma_commit(&kv_empty[prev_stage]);
+              if (ok && j < it.n_kv[g]) ok = issue_qk(g);
+            }
+          } else {
+            // Scores first (S_g is released as soon as it is in registers),
+            // then PV of the previous tile from the separate P columns.
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+              if (!ok || j >= it.n_kv[g]) continue;
               if (sc[g] > 0 && !mbar_wait(&s_free[g], (sc[g] - 1) & 1, abort_flag)) {
                 ok = false;
-                break;
+                continue;
               }
               tc_fence_after();
-              const uint32_t qa = q_addr + g * Cfg::kQBytes;
-              const uint32_t d_s = tmem_base + static_cast<uint32_t>(g * kTileK);
-#pragma unroll
-              for (int k = 0; k < HD / 16; ++k)
-                umma_ss(d_s, sdesc_sw128(qa + k * 32, 16, 1024),
-                        sdesc_sw128(k_addr + k * 32, 16, 1024), args.idesc_qk, k > 0 ? 1u : 0u);
-              umma_commit(&s_full[g]);
-              ++sc[g];
+              ok = issue_qk(g);
             }
-            if (!ok) break;
-            if (j == n - 1) umma_commit(&q_empty[slot]);
-          }
-          if (j >= 1) {
-            const int jp = j - 1;
-            const uint32_t v_addr = smem_u32(sKV + prev_stage * Cfg::kKVBytes) + kSub;
-            for (int g = 0; g < 2 && ok; ++g) {
-              if (jp >= it.n_kv[g]) continue;
-              if (!mbar_wait(&p_full[g], pvc[g] & 1, abort_flag)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              const uint32_t pa = tmem_base + Cfg::kPCol + g * (kTileK / 2);
-              const uint32_t d_o = tmem_base + Cfg::kOCol + g * HD;
 #pragma unroll
-              for (int k = 0; k < kTileK / 16; ++k)
-                umma_ts(d_o, pa + k * 8, sdesc_sw128(v_addr + k * 2048, kSub, 1024),
-                        args.idesc_pv, (jp > 0 || k > 0) ? 1u : 0u);
-              umma_commit(&pv_done[g]);
-              ++pvc[g];
-            }
-            if (!ok) break;
-            umma_commit(&kv_empty[prev_stage]);
+            for (int g = 0; g < 2; ++g)
+              if (ok && j >= 1 && j - 1 < it.n_kv[g]) ok = issue_pv(g, j - 1);
+            if (ok && j >= 1) umma_commit(&kv_empty[prev_stage]);
           }
+          if (!ok) break;
+          if (j == n - 1) umma_commit(&q_empty[slot]);
           if (j < n) {
             prev_stage = stage;
             if (++stage == kStages) {
@@ -643,7 +337,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const uint32_t s_col = static_cast<uint32_t>(g * kTileK);
     const uint32_t o_col = Cfg::kOCol + g * HD;
     const float sl2 = args.scale_log2;
-    const uint32_t p_col = Cfg::kPCol + g * (kTileK / 2);
+    const uint32_t p_col = Cfg::kPCol + g * Cfg::kPStride;
     uint32_t t = 0;  // tiles this group has processed (all items)
     bool ok = true;
     for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
@@ -676,9 +370,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
         for (int c = 0; c < kTileK / 32; ++c) tmem_ld32p(lane_base + s_col + c * 32, sv + c * 32);
         tmem_ld_wait_n<kTileK>(sv);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_free[g]);  // scores are in registers now
+        if constexpr (!Cfg::kAlias) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s_free[g]);  // scores are in registers now
+        }
         const int kv0 = j * kTileK;
         const bool need_mask = (args.causal && kv0 + kTileK - 1 > qs) ||
                                (kv0 + kTileK > it.kv_len) || use_key_mask;
@@ -736,8 +432,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const float rowsum = (sa0 + sa1) + (sb0 + sb1);
         l_i += rowsum;
         // The previous PV has read P and accumulated into O: P is free and O
-        // current.
-        if (t >= 1) {
+        // current.  With P over the score columns this is already implied:
+        // these scores were issued after that PV and commits complete in
+        // order.
+        if (!Cfg::kAlias && t >= 1) {
           w_ok = mbar_wait(&pv_done[g], (t - 1) & 1, abort_flag);
           if (!__all_sync(0xffffffffu, w_ok)) {
             ok = false;
@@ -804,22 +502,24 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   }
 }
 
-std::mutex g_attn_attr_mu;
-bool g_attn_attr_done[64][2];
+std::mutex g_pair_attr_mu;
+bool g_pair_attr_done[64][2];
 
 template <int HD>
-int launch_attn(const void* qkv, const AttnArgs& args, cudaStream_t stream) {
-  using Cfg = AttnCfg<HD>;
+int launch_attn_pair(const void* qkv, const AttnArgs& args, cudaStream_t stream) {
+  using Cfg = PairCfg<HD>;
   int dev = 0;
   cudaGetDevice(&dev);
   {
-    std::lock_guard<std::mutex> lock(g_attn_attr_mu);
+    std::lock_guard<std::mutex> lock(g_pair_attr_mu);
     const int slot = HD == 64 ? 0 : 1;
-    if (dev < 64 && !g_attn_attr_done[dev][slot]) {
-      if (const int fs = cuda_status(cudaFuncSetAttribute(attn_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(Cfg::kSmemBytes))))
-        return fs;
-      g_attn_attr_done[dev][slot] = true;
+    if (dev < 64 && !g_pair_attr_done[dev][slot]) {
+      for (auto fn : {attn_pair_kernel<HD, false>, attn_pair_kernel<HD, true>})
+        if (const int fs = cuda_status(cudaFuncSetAttribute(
+                fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                static_cast<int>(Cfg::kSmemBytes))))
+          return fs;
+      g_pair_attr_done[dev][slot] = true;
     }
   }
   CUtensorMap tm;
@@ -829,40 +529,12 @@ int launch_attn(const void* qkv, const AttnArgs& args, cudaStream_t stream) {
   const uint32_t box[3] = {64, 128, 1};
   const int st = make_tmap_16bit(&tm, 3, qkv, dims, strides, box, args.bf16 != 0);
   if (st != TJB_OK) return st;
-  dim3 grid(args.B * args.H, (args.S + kTileQ - 1) / kTileQ);
-  return launch_kernel(attn_fwd_kernel<HD>, grid, dim3(192), Cfg::kSmemBytes, stream, tm, args);
-}
-
-std::mutex g_pair_attr_mu;
-bool g_pair_attr_done[64];
-
-int launch_attn_pair(const void* qkv, const AttnArgs& args, cudaStream_t stream) {
-  int dev = 0;
-  cudaGetDevice(&dev);
-  {
-    std::lock_guard<std::mutex> lock(g_pair_attr_mu);
-    if (dev < 64 && !g_pair_attr_done[dev]) {
-      for (auto fn : {attn_pair_kernel<false>, attn_pair_kernel<true>})
-        if (const int fs = cuda_status(cudaFuncSetAttribute(
-                fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                static_cast<int>(PairCfg::kSmemBytes))))
-          return fs;
-      g_pair_attr_done[dev] = true;
-    }
-  }
-  CUtensorMap tm;
-  const uint64_t row = 3ull * args.H * PairCfg::HD;
-  const uint64_t dims[3] = {row, static_cast<uint64_t>(args.S), static_cast<uint64_t>(args.B)};
-  const uint64_t strides[2] = {row * 2, row * 2 * static_cast<uint64_t>(args.S)};
-  const uint32_t box[3] = {64, 128, 1};
-  const int st = make_tmap_16bit(&tm, 3, qkv, dims, strides, box, args.bf16 != 0);
-  if (st != TJB_OK) return st;
   const long total = static_cast<long>(args.B) * args.H * ((args.S + 2 * kTileQ - 1) / (2 * kTileQ));
   const int grid = static_cast<int>(total < num_sms() ? total : num_sms());
-  return args.bf16 ? launch_kernel(attn_pair_kernel<true>, dim3(grid), dim3(kPairThreads),
-                                PairCfg::kSmemBytes, stream, tm, args)
-                   : launch_kernel(attn_pair_kernel<false>, dim3(grid), dim3(kPairThreads),
-                                PairCfg::kSmemBytes, stream, tm, args);
+  return args.bf16 ? launch_kernel(attn_pair_kernel<HD, true>, dim3(grid), dim3(kPairThreads),
+                                Cfg::kSmemBytes, stream, tm, args)
+                   : launch_kernel(attn_pair_kernel<HD, false>, dim3(grid), dim3(kPairThreads),
+                                Cfg::kSmemBytes, stream, tm, args);
 }
 
 }  // namespace
@@ -893,5 +565,5 @@ extern "C" int tjb_flash_fwd(const void* qkv, void* out, int B, int S, int H, in
   a.idesc_qk = idesc_f16(kTileQ, kTileK, a.bf16 != 0, false);
   a.idesc_pv = idesc_f16(kTileQ, hd, a.bf16 != 0, true);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  return hd == 64 ? launch_attn_pair(qkv, a, s) : launch_attn<128>(qkv, a, s);
+  return hd == 64 ? launch_attn_pair<64>(qkv, a, s) : launch_attn_pair<128>(qkv, a, s);
 }
