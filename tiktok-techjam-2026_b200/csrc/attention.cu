@@ -77,11 +77,14 @@ struct PairCfg {
   // in order, so the next scores never overwrite an unread P).
   static constexpr bool kAlias = HD > 64;
   static constexpr int kQSlots = HD == 64 ? 2 : 1;
-  static constexpr int kStages = HD == 64 ? 4 : 2;
-  static constexpr uint32_t kQBytes = kSubs * kSub;       // one 128 x HD tile per group
-  static constexpr uint32_t kKVBytes = 2 * kSubs * kSub;  // K tile + V tile
+  // K and V tiles go through one ring of single-tile slots in the order
+  // K0 V0 K1 V1 ...; a slot is released as soon as its last reader is done,
+  // so K(j+1) loads while V(j) is still being read.
+  static constexpr int kSlots = HD == 64 ? 10 : 5;
+  static constexpr uint32_t kQBytes = kSubs * kSub;     // one 128 x HD tile per group
+  static constexpr uint32_t kTileBytes = kSubs * kSub;  // one K or V tile
   static constexpr uint32_t kSmemBytes =
-      1024 + 2 * kQSlots * kQBytes + kStages * kKVBytes + 256;
+      1024 + 2 * kQSlots * kQBytes + kSlots * kTileBytes + 512;
   // TMEM columns, head_dim 64: S0 [0,128) S1 [128,256) O0 [256,320)
   // O1 [320,384) P0 [384,448) P1 [448,512); head_dim 128: S0/P0 [0,128)
   // S1/P1 [128,256) O0 [256,384) O1 [384,512).  P: 128 x 128 16-bit, two
@@ -127,19 +130,19 @@ template <int HD, bool kBF16>
 __global__ void __launch_bounds__(kPairThreads, 1)
     attn_pair_kernel(const __grid_constant__ CUtensorMap tm, const AttnArgs args) {
   using Cfg = PairCfg<HD>;
-  constexpr int kStages = Cfg::kStages;
+  constexpr uint32_t kSlots = Cfg::kSlots;
   constexpr int kSubs = Cfg::kSubs;
   constexpr uint32_t kQSlots = Cfg::kQSlots;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sQ = smem;                                 // [slot][group][kQBytes]
-  uint8_t* sKV = sQ + 2 * kQSlots * Cfg::kQBytes;     // [kStages][K | V]
-  uint64_t* q_full = reinterpret_cast<uint64_t*>(sKV + kStages * Cfg::kKVBytes);  // [slot]
-  uint64_t* q_empty = q_full + 2;                                          // [slot]
+  uint8_t* sKV = sQ + 2 * kQSlots * Cfg::kQBytes;     // [kSlots][one K or V tile]
+  uint64_t* q_full = reinterpret_cast<uint64_t*>(sKV + kSlots * Cfg::kTileBytes);  // [slot]
+  uint64_t* q_empty = q_full + 2;                                           // [slot]
   uint64_t* kv_full = q_empty + 2;
-  uint64_t* kv_empty = kv_full + kStages;
-  uint64_t* s_full = kv_empty + kStages;  // [group]
+  uint64_t* kv_empty = kv_full + kSlots;
+  uint64_t* s_full = kv_empty + kSlots;  // [group]
   uint64_t* s_free = s_full + 2;          // [group]
   uint64_t* p_full = s_free + 2;          // [group]
   uint64_t* pv_done = p_full + 2;         // [group]
@@ -161,7 +164,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       mbar_init(&p_full[i], 4);
       mbar_init(&pv_done[i], 1);
     }
-    for (int s = 0; s < kStages; ++s) {
+    for (uint32_t s = 0; s < kSlots; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
@@ -185,8 +188,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // -------------------------------------------------------------- producer
-      int stage = 0;
-      uint32_t phase = 0, issued = 0, issued_parity = 0, n_items = 0;
+      uint32_t seq = 0, n_items = 0;  // K/V tiles issued, items started
       bool ok = true;
       for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
         const PairItem it = decode_pair(w, args, num_pairs, prefix);
@@ -208,126 +210,124 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         ++n_items;
         const int colK = (args.H + it.h) * HD;
         const int colV = (2 * args.H + it.h) * HD;
-        for (int j = 0; j < n; ++j) {
-          if (!mbar_wait(&kv_empty[stage], phase ^ 1, abort_flag)) {
+        for (int t = 0; t < 2 * n && ok; ++t, ++seq) {
+          const uint32_t slot = seq % kSlots;
+          if (!mbar_wait(&kv_empty[slot], ((seq / kSlots) & 1) ^ 1, abort_flag)) {
             ok = false;
             break;
           }
-          uint8_t* sK = sKV + stage * Cfg::kKVBytes;
-          mbar_arrive_expect_tx(&kv_full[stage], Cfg::kKVBytes);
-          for (int sub = 0; sub < kSubs; ++sub) {
-            tma_load_3d(sK + sub * kSub, &tm, &kv_full[stage], colK + sub * 64, j * kTileK, it.b);
-            tma_load_3d(sK + (kSubs + sub) * kSub, &tm, &kv_full[stage], colV + sub * 64,
-                        j * kTileK, it.b);
-          }
-          issued |= 1u << stage;
-          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1;
-          }
+          uint8_t* dst = sKV + slot * Cfg::kTileBytes;
+          const int col = (t & 1) ? colV : colK;
+          mbar_arrive_expect_tx(&kv_full[slot], Cfg::kTileBytes);
+          for (int sub = 0; sub < kSubs; ++sub)
+            tma_load_3d(dst + sub * kSub, &tm, &kv_full[slot], col + sub * 64, (t >> 1) * kTileK,
+                        it.b);
         }
       }
+      // Let every load still in flight land before the CTA exits.
       for (uint32_t k = n_items >= kQSlots ? n_items - kQSlots : 0; k < n_items; ++k)
         mbar_wait_drain(&q_full[k % kQSlots], (k / kQSlots) & 1);
-      for (int s = 0; s < kStages; ++s)
-        if ((issued >> s) & 1u) mbar_wait_drain(&kv_full[s], (issued_parity >> s) & 1u);
+      for (uint32_t k = seq >= kSlots ? seq - kSlots : 0; k < seq; ++k)
+        mbar_wait_drain(&kv_full[k % kSlots], (k / kSlots) & 1);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ MMA issuer
-      const uint32_t q_base = smem_u32(sQ);
-      int stage = 0, prev_stage = 0;
-      uint32_t phase = 0, n_items = 0;
-      uint32_t sc[2] = {0, 0}, pvc[2] = {0, 0};
-      bool ok = true;
-      for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
-        const PairItem it = decode_pair(w, args, num_pairs, prefix);
-        const int n = max(it.n_kv[0], it.n_kv[1]);
-        if (n == 0) continue;
-        const uint32_t slot = n_items % kQSlots;
-        if (!mbar_wait(&q_full[slot], (n_items / kQSlots) & 1, abort_flag)) break;
-        ++n_items;
-        const uint32_t q_addr = q_base + slot * 2 * Cfg::kQBytes;
-        for (int j = 0; j <= n && ok; ++j) {
-          const uint32_t k_addr = smem_u32(sKV + stage * Cfg::kKVBytes);
-          const uint32_t v_addr = smem_u32(sKV + prev_stage * Cfg::kKVBytes) + kSubs * kSub;
-          bool k_ready = j >= n;
-          // S_g = Q_g K_j^T (HD/16 K-steps over kSubs 64-column sub-tiles).
-          auto issue_qk = [&](int g) {
-            if (!k_ready) {
-              if (!mbar_wait(&kv_full[stage], phase, abort_flag)) return false;
-              tc_fence_after();
-              k_ready = true;
-            }
-            const uint32_t qa = q_addr + g * Cfg::kQBytes;
-            const uint32_t d_s = tmem_base + static_cast<uint32_t>(g * kTileK);
-#pragma unroll
-            for (int k = 0; k < HD / 16; ++k) {
-              const uint32_t off = (k >> 2) * kSub + (k & 3) * 32;
-              umma_ss(d_s, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(k_addr + off, 16, 1024),
-                      args.idesc_qk, k > 0 ? 1u : 0u);
-            }
-            umma_commit(&s_full[g]);
-            ++sc[g];
-            return true;
-          };
-          // O_g += P_g V_{j-1}, P_g read from tensor memory.
-          auto issue_pv = [&](int g, int jp) {
-            if (!mbar_wait(&p_full[g], pvc[g] & 1, abort_flag)) return false;
+    // ------------------------------------------------------------ MMA issuer
+    // The whole warp runs this loop, converged; one elected lane issues.
+    const uint32_t q_base = smem_u32(sQ);
+    uint32_t n_items = 0, base = 0;  // base: ring sequence number of the item's K(0)
+    uint32_t sc[2] = {0, 0}, pvc[2] = {0, 0};
+    bool ok = true;
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+    };
+    for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+      const PairItem it = decode_pair(w, args, num_pairs, prefix);
+      const int n = max(it.n_kv[0], it.n_kv[1]);
+      if (n == 0) continue;
+      const uint32_t slot = n_items % kQSlots;
+      if (!wait(&q_full[slot], (n_items / kQSlots) & 1)) break;
+      ++n_items;
+      const uint32_t q_addr = q_base + slot * 2 * Cfg::kQBytes;
+      for (int j = 0; j <= n && ok; ++j) {
+        const uint32_t kseq = base + 2 * j, vseq = kseq - 1;  // K(j), V(j-1)
+        const uint32_t kslot = kseq % kSlots, vslot = vseq % kSlots;
+        const uint32_t k_addr = smem_u32(sKV + kslot * Cfg::kTileBytes);
+        const uint32_t v_addr = smem_u32(sKV + vslot * Cfg::kTileBytes);
+        bool k_ready = j >= n, v_ready = j == 0;
+        // S_g = Q_g K_j^T (HD/16 K-steps over kSubs 64-column sub-tiles).
+        auto issue_qk = [&](int g) {
+          if (!k_ready) {
+            if (!wait(&kv_full[kslot], (kseq / kSlots) & 1)) return false;
             tc_fence_after();
-            const uint32_t pa = tmem_base + Cfg::kPCol + g * Cfg::kPStride;
-            const uint32_t d_o = tmem_base + Cfg::kOCol + g * HD;
-#pragma unroll
-            for (int k = 0; k < kTileK / 16; ++k)
-              umma_ts(d_o, pa + k * 8, sdesc_sw128(v_addr + k * 2048, kSub, 1024),
-                      args.idesc_pv, (jp > 0 || k > 0) ? 1u : 0u);
-            umma_commit(&pv_done[g]);
-            ++pvc[g];
-            return true;
-          };
-          if constexpr (Cfg::kAlias) {
-            // Per group: PV of tile j-1 (reads P out of the score columns),
-            // then QK of tile j into the same columns.  The stage of tile j-1
-            // is released once both PVs are issued.
-#pragma unroll
-            for (int g = 0; g < 2; ++g) {
-              if (ok && j >= 1 && j - 1 < it.n_kv[g]) ok = issue_pv(g, j - 1);
-              if (ok && g == 1 && j >= 1) umma_commit(&kv_empty[prev_stage]);
-              if (ok && j < it.n_kv[g]) ok = issue_qk(g);
-            }
-          } else {
-            // Scores first (S_g is released as soon as it is in registers),
-            // then PV of the previous tile from the separate P columns.
-#pragma unroll
-            for (int g = 0; g < 2; ++g) {
-              if (!ok || j >= it.n_kv[g]) continue;
-              if (sc[g] > 0 && !mbar_wait(&s_free[g], (sc[g] - 1) & 1, abort_flag)) {
-                ok = false;
-                continue;
-              }
-              tc_fence_after();
-              ok = issue_qk(g);
-            }
-#pragma unroll
-            for (int g = 0; g < 2; ++g)
-              if (ok && j >= 1 && j - 1 < it.n_kv[g]) ok = issue_pv(g, j - 1);
-            if (ok && j >= 1) umma_commit(&kv_empty[prev_stage]);
+            k_ready = true;
           }
-          if (!ok) break;
-          if (j == n - 1) umma_commit(&q_empty[slot]);
-          if (j < n) {
-            prev_stage = stage;
-            if (++stage == kStages) {
-              stage = 0;
-              phase ^= 1;
-            }
+          const uint32_t qa = q_addr + g * Cfg::kQBytes;
+          const uint32_t d_s = tmem_base + static_cast<uint32_t>(g * kTileK);
+#pragma unroll
+          for (int k = 0; k < HD / 16; ++k) {
+            const uint32_t off = (k >> 2) * kSub + (k & 3) * 32;
+            umma_ss_w(d_s, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(k_addr + off, 16, 1024),
+                    args.idesc_qk, k > 0 ? 1u : 0u);
           }
+          umma_commit_w(&s_full[g]);
+          ++sc[g];
+          return true;
+        };
+        // O_g += P_g V_{j-1}, P_g read from tensor memory.
+        auto issue_pv = [&](int g, int jp) {
+          if (!v_ready) {
+            if (!wait(&kv_full[vslot], (vseq / kSlots) & 1)) return false;
+            v_ready = true;
+          }
+          if (!wait(&p_full[g], pvc[g] & 1)) return false;
+          tc_fence_after();
+          const uint32_t pa = tmem_base + Cfg::kPCol + g * Cfg::kPStride;
+          const uint32_t d_o = tmem_base + Cfg::kOCol + g * HD;
+#pragma unroll
+          for (int k = 0; k < kTileK / 16; ++k)
+            umma_ts_w(d_o, pa + k * 8, sdesc_sw128(v_addr + k * 2048, kSub, 1024),
+                    args.idesc_pv, (jp > 0 || k > 0) ? 1u : 0u);
+          umma_commit_w(&pv_done[g]);
+          ++pvc[g];
+          return true;
+        };
+        if constexpr (Cfg::kAlias) {
+          // Per group: PV of tile j-1 (reads P out of the score columns),
+          // then QK of tile j into the same columns.  V(j-1) is released
+          // once both PVs are issued, K(j) once both QKs are.
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            if (ok && j >= 1 && j - 1 < it.n_kv[g]) ok = issue_pv(g, j - 1);
+            if (ok && g == 1 && j >= 1) umma_commit_w(&kv_empty[vslot]);
+            if (ok && j < it.n_kv[g]) ok = issue_qk(g);
+          }
+          if (ok && j < n) umma_commit_w(&kv_empty[kslot]);
+        } else {
+          // Scores first (S_g is released as soon as it is in registers),
+          // then PV of the previous tile from the separate P columns.
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            if (!ok || j >= it.n_kv[g]) continue;
+            if (sc[g] > 0 && !wait(&s_free[g], (sc[g] - 1) & 1)) {
+              ok = false;
+              continue;
+            }
+            tc_fence_after();
+            ok = issue_qk(g);
+          }
+          if (ok && j < n) umma_commit_w(&kv_empty[kslot]);
+#pragma unroll
+          for (int g = 0; g < 2; ++g)
+            if (ok && j >= 1 && j - 1 < it.n_kv[g]) ok = issue_pv(g, j - 1);
+          if (ok && j >= 1) umma_commit_w(&kv_empty[vslot]);
         }
+        if (!ok) break;
+        if (j == n - 1) umma_commit_w(&q_empty[slot]);
       }
-      umma_commit(drain);
-      mbar_wait_drain(drain, 0);
+      base += 2 * n;
     }
+    umma_commit_w(drain);
+    mbar_wait_drain(drain, 0);
   } else {
     // -------------------------------------------------------------- softmax
     const int g = (warp - 2) >> 2;  // group 0: warps 2-5, group 1: warps 6-9
@@ -379,12 +379,18 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const bool need_mask = (args.causal && kv0 + kTileK - 1 > qs) ||
                                (kv0 + kTileK > it.kv_len) || use_key_mask;
         if (need_mask) {
+          // Keys [kv0, kv0 + lim) of this row survive the causal and length
+          // limits; c < lim compares against an immediate per column.
+          const int lim = (args.causal ? min(it.kv_len, qi + 1) : it.kv_len) - kv0;
 #pragma unroll
-          for (int c = 0; c < kTileK; ++c) {
-            const int kj = kv0 + c;
-            bool masked = kj >= it.kv_len || (args.causal && kj > qi);
-            if (km != nullptr && kj < args.S && km[kj] == 0) masked = true;
-            if (masked) sv[c] = __float_as_uint(-INFINITY);
+          for (int c = 0; c < kTileK; ++c)
+            sv[c] = c < lim ? sv[c] : __float_as_uint(-INFINITY);
+          if (km != nullptr) {
+#pragma unroll
+            for (int c = 0; c < kTileK; ++c) {
+              const int kj = kv0 + c;
+              if (kj < args.S && km[kj] == 0) sv[c] = __float_as_uint(-INFINITY);
+            }
           }
         }
         // Row max: eight independent three-input max chains, then combine.
