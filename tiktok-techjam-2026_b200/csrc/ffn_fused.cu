@@ -166,88 +166,90 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
         if ((issued >> s) & 1u) mbar_wait_drain(&full[s], (issued_parity >> s) & 1u);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------------------------------------------------- MMA issuer
-      const uint32_t hb = smem_u32(hbuf);
-      int stage = 0;
-      uint32_t phase = 0, g1c = 0, g2c = 0, tc = 0;
-      bool ok = true;
-      for (int t = cid; t < num_m && ok; t += n_clusters) {
-        for (int j = 0; j <= NJ && ok; ++j) {
-          if (j < NJ) {
-            const uint32_t buf = g1c & 1;
-            if (!mbar_wait(&g1_empty[buf], ((g1c >> 1) & 1) ^ 1, abort_flag)) {
+    // ---------------------------------------------------------- MMA issuer
+    // The whole warp runs this loop, converged; one elected lane issues.
+    const uint32_t hb = smem_u32(hbuf);
+    int stage = 0;
+    uint32_t phase = 0, g1c = 0, g2c = 0, tc = 0;
+    bool ok = true;
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+    };
+    for (int t = cid; t < num_m && ok; t += n_clusters) {
+      for (int j = 0; j <= NJ && ok; ++j) {
+        if (j < NJ) {
+          const uint32_t buf = g1c & 1;
+          if (!wait(&g1_empty[buf], ((g1c >> 1) & 1) ^ 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d_g = tmem_base + kG1Col + buf * 128;
+          for (int kb = 0; kb < nk1; ++kb) {
+            if (!wait(&full[stage], phase)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t d_g = tmem_base + kG1Col + buf * 128;
-            for (int kb = 0; kb < nk1; ++kb) {
-              if (!mbar_wait(&full[stage], phase, abort_flag)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              const uint32_t a0 = smem_u32(ring + stage * kFStage);
+            const uint32_t a0 = smem_u32(ring + stage * kFStage);
 #pragma unroll
-              for (int k = 0; k < 4; ++k)
-                umma_ss(d_g, sdesc_sw128(a0 + k * 32, 16, 1024),
+            for (int k = 0; k < 4; ++k)
+              umma_ss_w(d_g, sdesc_sw128(a0 + k * 32, 16, 1024),
                         sdesc_sw128(a0 + kFSub + k * 32, 16, 1024), args.idesc1,
                         (kb | k) != 0 ? 1u : 0u);
-              umma_commit(&empty[stage]);
-              if (++stage == S) {
-                stage = 0;
-                phase ^= 1;
-              }
+            umma_commit_w(&empty[stage]);
+            if (++stage == S) {
+              stage = 0;
+              phase ^= 1;
             }
-            if (!ok) break;
-            umma_commit(&g1_full[buf]);
-            ++g1c;
           }
-          if (j >= 1) {
-            // All C slices of hidden chunk j-1 are in this CTA's buffer.
-            if (!mbar_wait_cluster(h_ready, g2c & 1, abort_flag)) {
+          if (!ok) break;
+          umma_commit_w(&g1_full[buf]);
+          ++g1c;
+        }
+        if (j >= 1) {
+          // All C slices of hidden chunk j-1 are in this CTA's buffer.
+          if (!__all_sync(0xffffffffu, mbar_wait_cluster(h_ready, g2c & 1, abort_flag))) {
+            ok = false;
+            break;
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          tc_fence_after();
+          if (j == 1 && !wait(o_empty, (tc & 1) ^ 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int kb = 0; kb < nk2; ++kb) {
+            if (!wait(&full[stage], phase)) {
               ok = false;
               break;
             }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             tc_fence_after();
-            if (j == 1 && !mbar_wait(o_empty, (tc & 1) ^ 1, abort_flag)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            for (int kb = 0; kb < nk2; ++kb) {
-              if (!mbar_wait(&full[stage], phase, abort_flag)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              const uint32_t b0 = smem_u32(ring + stage * kFStage);
-              const uint32_t a0 = hb + kb * kFSub;
+            const uint32_t b0 = smem_u32(ring + stage * kFStage);
+            const uint32_t a0 = hb + kb * kFSub;
 #pragma unroll
-              for (int k = 0; k < 4; ++k)
-                umma_ss(tmem_base + kOCol, sdesc_sw128(a0 + k * 32, 16, 1024),
+            for (int k = 0; k < 4; ++k)
+              umma_ss_w(tmem_base + kOCol, sdesc_sw128(a0 + k * 32, 16, 1024),
                         sdesc_sw128(b0 + k * 32, 16, 1024), args.idesc2,
                         (j > 1 || kb > 0 || k > 0) ? 1u : 0u);
-              umma_commit(&empty[stage]);
-              if (++stage == S) {
-                stage = 0;
-                phase ^= 1;
-              }
+            umma_commit_w(&empty[stage]);
+            if (++stage == S) {
+              stage = 0;
+              phase ^= 1;
             }
-            if (!ok) break;
-            umma_commit(g2_done);
-            ++g2c;
           }
+          if (!ok) break;
+          umma_commit_w(g2_done);
+          ++g2c;
         }
-        if (!ok) break;
-        umma_commit(o_full);
-        ++tc;
       }
-      umma_commit(drain);
-      mbar_wait_drain(drain, 0);
+      if (!ok) break;
+      umma_commit_w(o_full);
+      ++tc;
     }
+    umma_commit_w(drain);
+    mbar_wait_drain(drain, 0);
   } else if (warp == 2) {
     if (lane == 0) {
       // ------------------------------------------------ cluster relay of h_free

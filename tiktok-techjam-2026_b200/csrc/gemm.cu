@@ -190,45 +190,47 @@ __global__ void __launch_bounds__(192, 1)
         if ((issued >> s) & 1u) mbar_wait_drain(&full[s], (issued_parity >> s) & 1u);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------------------------------------------------- MMA issuer
-      int stage = 0, acc = 0;
-      uint32_t phase = 0, acc_phase = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < num_k; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + stage * Cfg::kABytes);
-          const uint32_t b0 = smem_u32(sB + stage * Cfg::kBBytes);
-#pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            umma_ss(d_tmem, sdesc_sw128(a0 + k * 32, 16, 1024), sdesc_sw128(b0 + k * 32, 16, 1024),
-                    args.idesc, (kb | k) != 0 ? 1u : 0u);
-          }
-          umma_commit(&empty[stage]);
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1;
-          }
+    // ---------------------------------------------------------- MMA issuer
+    // The whole warp runs this loop, converged; one elected lane issues.
+    int stage = 0, acc = 0;
+    uint32_t phase = 0, acc_phase = 0;
+    bool ok = true;
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+    };
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      if (!wait(&tempty[acc], acc_phase ^ 1)) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+      for (int kb = 0; kb < num_k; ++kb) {
+        if (!wait(&full[stage], phase)) {
+          ok = false;
+          break;
         }
-        if (!ok) break;
-        umma_commit(&tfull[acc]);
-        if (++acc == 2) {
-          acc = 0;
-          acc_phase ^= 1;
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sA + stage * Cfg::kABytes);
+        const uint32_t b0 = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k) {
+          umma_ss_w(d_tmem, sdesc_sw128(a0 + k * 32, 16, 1024),
+                    sdesc_sw128(b0 + k * 32, 16, 1024), args.idesc, (kb | k) != 0 ? 1u : 0u);
+        }
+        umma_commit_w(&empty[stage]);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1;
         }
       }
-      // All issued MMAs retire before tensor memory is released.
-      umma_commit(drain);
-      mbar_wait_drain(drain, 0);
+      if (!ok) break;
+      umma_commit_w(&tfull[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
     }
+    // All issued MMAs retire before tensor memory is released.
+    umma_commit_w(drain);
+    mbar_wait_drain(drain, 0);
   } else {
     // -------------------------------------------------------------- epilogue
     const int quad = warp & 3;  // TMEM lanes this warp may access
