@@ -136,6 +136,21 @@ int tjb_flash_fwd(const void* qkv, void* out, int B, int S, int H, int hd,
                   int dtype, tjb_stream_t stream);
 
 /*
+ * tjb_flash_fwd with work items handed out dynamically: CTAs claim
+ * (batch*head, query-tile pair) items, heaviest causal rows first, from the
+ * counter at sched[0], so ragged prefix lengths do not leave SMs idle.
+ * sched: two int32 in device memory, 8-byte aligned, both zero before the
+ * call; the kernel leaves them zero again when it completes, so one pair
+ * serves any number of calls that run one after another (same stream, or a
+ * CUDA graph).  Calls that may run at the same time need separate pairs.
+ * No counterpart in the reference (its Triton grid is static).
+ */
+int tjb_flash_fwd_sched(const void* qkv, void* out, int B, int S, int H, int hd,
+                        float scale, int causal, const int32_t* lengths,
+                        const uint8_t* key_mask, const int32_t* mask_flags,
+                        int dtype, int32_t* sched, tjb_stream_t stream);
+
+/*
  * Feed-forward block out = gelu_erf(h * w1^T + b1) * w2^T + b2.
  * h: [T, d]; w1: [F, d]; w2: [d, F] (nn.Linear layouts, f16/bf16);
  * b1: fp32 [F]; b2: fp32 [d]; out: out_dtype [T, d].

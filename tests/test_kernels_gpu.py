@@ -183,6 +183,33 @@ def test_flash_general_key_mask(hd):
     assert torch.isfinite(out).all()
 
 
+@pytest.mark.parametrize("hd", [64, 128])
+@pytest.mark.parametrize("mask_kind", ["none", "prefix", "general"])
+def test_flash_dynamic_schedule_matches_static(hd, mask_kind):
+    """Items handed out from the device counter give the same bits as the
+    fixed stride (each item is computed the same way whichever CTA takes it),
+    and every launch leaves the counter at zero for the next one."""
+    b, s, h = 5, 900, 4
+    g = torch.Generator(device=DEV).manual_seed(hd + len(mask_kind))
+    qkv = torch.randn(b, s, 3, h, hd, device=DEV, generator=g).half()
+    kw = {}
+    if mask_kind != "none":
+        if mask_kind == "prefix":
+            lengths = torch.tensor([900, 1, 300, 0, 641], dtype=torch.int32, device=DEV)
+            mask = torch.arange(s, device=DEV)[None, :] < lengths[:, None]
+        else:
+            mask = torch.rand(b, s, device=DEV, generator=g) > 0.4
+            mask[:, 0] = True
+        lens, flags = K().mask_lengths(mask)
+        kw = dict(lengths=lens, key_mask=mask.to(torch.uint8), mask_flags=flags)
+    ref = K().flash_attention(qkv, h, causal=True, **kw)
+    sched = torch.zeros(2, dtype=torch.int32, device=DEV)
+    for _ in range(3):
+        out = K().flash_attention(qkv, h, causal=True, sched=sched, **kw)
+        assert torch.equal(out, ref)
+        assert sched.tolist() == [0, 0]
+
+
 def test_flash_unsupported_head_dim():
     from tjkernels._lib import KernelError
     qkv = torch.randn(1, 64, 3, 4, 32, device=DEV).bfloat16()

@@ -40,6 +40,7 @@ constexpr uint32_t kSub = 128 * 64 * 2;  // one 128-row x 64-column 16-bit sub-t
 
 struct AttnArgs {
   void* out;
+  int32_t* sched;  // [next item, CTAs done]: dynamic work queue, or null for a static one
   const int32_t* lengths;
   const uint8_t* key_mask;
   const int32_t* mask_flags;
@@ -64,6 +65,7 @@ __device__ __forceinline__ float fast_exp2(float x) {
 // below 256 in 16-bit, every sum stays in fp32 range); O / l is exact for any
 // choice of the reference max.
 constexpr int kPairThreads = 320;
+constexpr int kItemSlots = 4;  // work items queued from the producer to the other warps
 constexpr float kRescaleLog2 = 8.0f;
 
 template <int HD_>
@@ -147,7 +149,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint64_t* p_full = s_free + 2;          // [group]
   uint64_t* pv_done = p_full + 2;         // [group]
   uint64_t* drain = pv_done + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* item_full = drain + 1;                 // [kItemSlots]
+  uint64_t* item_empty = item_full + kItemSlots;   // [kItemSlots]
+  volatile int* item_q = reinterpret_cast<volatile int*>(item_empty + kItemSlots);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_empty + kItemSlots) + kItemSlots;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -169,6 +174,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       mbar_init(&kv_empty[s], 1);
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < kItemSlots; ++i) {
+      mbar_init(&item_full[i], 1);
+      mbar_init(&item_empty[i], 1 + 8);  // the MMA warp and the eight softmax warps
+    }
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tm);
@@ -190,7 +199,20 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       // -------------------------------------------------------------- producer
       uint32_t seq = 0, n_items = 0;  // K/V tiles issued, items started
       bool ok = true;
-      for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+      for (uint32_t qn = 0;; ++qn) {
+        // Claim the next work item (from the shared counter, heaviest causal
+        // rows first, or a fixed stride without one) and queue it for the
+        // MMA and softmax warps; -1 ends their loops.
+        int w = args.sched != nullptr ? atomicAdd(args.sched, 1)
+                                      : static_cast<int>(blockIdx.x + qn * gridDim.x);
+        if (w >= total || !ok) w = -1;
+        const uint32_t islot = qn % kItemSlots;
+        if (qn >= kItemSlots &&
+            !mbar_wait(&item_empty[islot], (qn / kItemSlots - 1) & 1, abort_flag))
+          break;
+        item_q[islot] = w;
+        mbar_arrive(&item_full[islot]);
+        if (w < 0) break;
         const PairItem it = decode_pair(w, args, num_pairs, prefix);
         const int n = max(it.n_kv[0], it.n_kv[1]);
         if (n == 0) continue;
@@ -240,7 +262,13 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     auto wait = [&](uint64_t* bar, uint32_t parity) {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
     };
-    for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+    for (uint32_t qn = 0; ok; ++qn) {
+      const uint32_t islot = qn % kItemSlots;
+      if (!wait(&item_full[islot], (qn / kItemSlots) & 1)) break;
+      const int w = item_q[islot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[islot]);
+      if (w < 0) break;
       const PairItem it = decode_pair(w, args, num_pairs, prefix);
       const int n = max(it.n_kv[0], it.n_kv[1]);
       if (n == 0) continue;
@@ -340,7 +368,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const uint32_t p_col = Cfg::kPCol + g * Cfg::kPStride;
     uint32_t t = 0;  // tiles this group has processed (all items)
     bool ok = true;
-    for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+    for (uint32_t qn = 0; ok; ++qn) {
+      const uint32_t islot = qn % kItemSlots;
+      if (!__all_sync(0xffffffffu, mbar_wait(&item_full[islot], (qn / kItemSlots) & 1, abort_flag)))
+        break;
+      const int w = item_q[islot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[islot]);
+      if (w < 0) break;
       const PairItem it = decode_pair(w, args, num_pairs, prefix);
       const int qs = it.q0 + g * kTileQ;
       const int qi = qs + r;
@@ -506,6 +541,16 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
+  // The last CTA out returns the work counter to zero for the next launch
+  // (every CTA has made its final claim before it counts itself done).
+  if (threadIdx.x == 0 && args.sched != nullptr) {
+    __threadfence();
+    if (atomicAdd(args.sched + 1, 1) == static_cast<int>(gridDim.x) - 1) {
+      atomicExch(args.sched, 0);
+      atomicExch(args.sched + 1, 0);
+      __threadfence();
+    }
+  }
 }
 
 std::mutex g_pair_attr_mu;
@@ -546,18 +591,22 @@ int launch_attn_pair(const void* qkv, const AttnArgs& args, cudaStream_t stream)
 }  // namespace
 }  // namespace tjb
 
-extern "C" int tjb_flash_fwd(const void* qkv, void* out, int B, int S, int H, int hd, float scale,
-                             int causal, const int32_t* lengths, const uint8_t* key_mask,
-                             const int32_t* mask_flags, int dtype, tjb_stream_t stream) {
-  using namespace tjb;
+namespace tjb {
+namespace {
+int flash_fwd(const void* qkv, void* out, int B, int S, int H, int hd, float scale, int causal,
+              const int32_t* lengths, const uint8_t* key_mask, const int32_t* mask_flags,
+              int dtype, int32_t* sched, tjb_stream_t stream) {
   if (!qkv || !out || B <= 0 || S <= 0 || H <= 0 || hd <= 0) return TJB_ERR_INVALID_ARGUMENT;
   if (dtype != TJB_F16 && dtype != TJB_BF16) return TJB_ERR_UNSUPPORTED_DTYPE;
   if (hd != 64 && hd != 128) return TJB_ERR_BAD_SHAPE;
   if (B * H > 2147483647 / 2 || (S + kTileQ - 1) / kTileQ > 65535) return TJB_ERR_BAD_SHAPE;
   if (!aligned16(qkv) || !aligned16(out)) return TJB_ERR_BAD_ALIGNMENT;
+  if (sched != nullptr && (reinterpret_cast<uintptr_t>(sched) & 7u) != 0)
+    return TJB_ERR_BAD_ALIGNMENT;
   if (!device_ok()) return TJB_ERR_NO_DEVICE;
   AttnArgs a;
   a.out = out;
+  a.sched = sched;
   a.lengths = lengths;
   a.key_mask = key_mask;
   a.mask_flags = mask_flags;
@@ -572,4 +621,22 @@ extern "C" int tjb_flash_fwd(const void* qkv, void* out, int B, int S, int H, in
   a.idesc_pv = idesc_f16(kTileQ, hd, a.bf16 != 0, true);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   return hd == 64 ? launch_attn_pair<64>(qkv, a, s) : launch_attn_pair<128>(qkv, a, s);
+}
+}  // namespace
+}  // namespace tjb
+
+extern "C" int tjb_flash_fwd(const void* qkv, void* out, int B, int S, int H, int hd, float scale,
+                             int causal, const int32_t* lengths, const uint8_t* key_mask,
+                             const int32_t* mask_flags, int dtype, tjb_stream_t stream) {
+  return tjb::flash_fwd(qkv, out, B, S, H, hd, scale, causal, lengths, key_mask, mask_flags,
+                        dtype, nullptr, stream);
+}
+
+extern "C" int tjb_flash_fwd_sched(const void* qkv, void* out, int B, int S, int H, int hd,
+                                   float scale, int causal, const int32_t* lengths,
+                                   const uint8_t* key_mask, const int32_t* mask_flags, int dtype,
+                                   int32_t* sched, tjb_stream_t stream) {
+  if (sched == nullptr) return TJB_ERR_INVALID_ARGUMENT;
+  return tjb::flash_fwd(qkv, out, B, S, H, hd, scale, causal, lengths, key_mask, mask_flags,
+                        dtype, sched, stream);
 }

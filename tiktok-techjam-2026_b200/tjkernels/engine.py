@@ -84,6 +84,9 @@ class Engine:
         self.final_ln: Optional[Tuple[torch.Tensor, torch.Tensor, float]] = None
         self._module = module
         self._graphs = GraphCache()
+        # Work counter of the dynamic attention schedule: zero between calls
+        # (each launch returns it to zero), reused by every layer in order.
+        self._attn_sched: Optional[torch.Tensor] = None
 
     # ---------------------------------------------------------------- weights
 
@@ -121,6 +124,7 @@ class Engine:
             self.final_ln = (fn.weight.float().contiguous(), fn.bias.float().contiguous(),
                              fn.eps)
         self.layers = layers
+        self._attn_sched = torch.zeros(2, dtype=torch.int32, device=self.device)
         self._built_for = key
         self._graphs.clear()
 
@@ -155,7 +159,8 @@ class Engine:
             qkv = K.gemm_bias(h, lw.wqkv, lw.bqkv, m_tiles=tiles)
             ctx = K.flash_attention(qkv.view(batch, seq, 3, heads, hd), heads,
                                     causal=self.causal, lengths=lengths, key_mask=mask_u8,
-                                    mask_flags=flags, scale=self.scale)
+                                    mask_flags=flags, scale=self.scale,
+                                    sched=self._attn_sched if plan.attn_dynamic else None)
             attn_out = K.gemm_bias(ctx, lw.wo, lw.bo, out_dtype=plan.delta_dtype, m_tiles=tiles)
             res, h2 = K.fused_add_layernorm(
                 res, attn_out, lw.ln2_w, lw.ln2_b, lw.ln2_eps, out_dtype=plan.compute_dtype,

@@ -168,9 +168,15 @@ def flash_attention(qkv: torch.Tensor, heads: int, causal: bool = True,
                     lengths: Optional[torch.Tensor] = None,
                     key_mask: Optional[torch.Tensor] = None,
                     mask_flags: Optional[torch.Tensor] = None,
-                    scale: Optional[float] = None) -> torch.Tensor:
-    """qkv ``[B, S, 3, H, hd]`` (contiguous) -> out ``[B*S, H*hd]``."""
-    _need_cuda(qkv, lengths, key_mask, mask_flags)
+                    scale: Optional[float] = None,
+                    sched: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """qkv ``[B, S, 3, H, hd]`` (contiguous) -> out ``[B*S, H*hd]``.
+
+    ``sched``: optional int32 ``[2]`` device tensor, zero, that switches to
+    the dynamic work queue (``tjb_flash_fwd_sched``); the kernel leaves it
+    zero again.  Calls that may overlap on the GPU need separate tensors.
+    """
+    _need_cuda(qkv, lengths, key_mask, mask_flags, sched)
     b, s, three, h, hd = qkv.shape
     if three != 3 or h != heads:
         raise ValueError("qkv must be [B, S, 3, H, hd]")
@@ -178,6 +184,15 @@ def flash_attention(qkv: torch.Tensor, heads: int, causal: bool = True,
         raise ValueError("qkv must be contiguous")
     out = torch.empty((b * s, h * hd), dtype=qkv.dtype, device=qkv.device)
     scale = hd ** -0.5 if scale is None else scale
+    if sched is not None:
+        if sched.dtype != torch.int32 or sched.numel() < 2:
+            raise ValueError("sched must be an int32 tensor of two elements")
+        status = _lib.lib().tjb_flash_fwd_sched(
+            _ptr(qkv), _ptr(out), b, s, h, hd, float(scale), int(causal), _ptr(lengths),
+            _ptr(key_mask), _ptr(mask_flags), _code(qkv.dtype), _ptr(sched),
+            _stream(qkv.device))
+        _lib.check(status, "tjb_flash_fwd_sched")
+        return out
     status = _lib.lib().tjb_flash_fwd(
         _ptr(qkv), _ptr(out), b, s, h, hd, float(scale), int(causal), _ptr(lengths),
         _ptr(key_mask), _ptr(mask_flags), _code(qkv.dtype), _stream(qkv.device))

@@ -54,6 +54,10 @@ class Plan:
     # d_model 1024 (its shared-memory hidden chunk leaves room for only a
     # 3-stage operand ring).
     ffn_single_kernel: bool = False
+    # Hand attention work items out from a device counter (heaviest causal
+    # rows first) instead of a fixed stride over the CTAs, so that ragged
+    # prefix lengths do not leave SMs idle.
+    attn_dynamic: bool = True
     label: str = "default"
 
     def to_json(self) -> Dict[str, object]:
@@ -64,6 +68,7 @@ class Plan:
             "cuda_graph": self.cuda_graph,
             "skip_padding": self.skip_padding,
             "ffn_single_kernel": self.ffn_single_kernel,
+            "attn_dynamic": self.attn_dynamic,
             "label": self.label,
         }
 
@@ -144,6 +149,8 @@ def select_plan(batch: int, seq: int, d_model: int, heads: int, ffn_dim: int, la
         plan = replace(plan, ffn_single_kernel=True)
     if os.environ.get("TJ_NO_SKIP") == "1":
         plan = replace(plan, skip_padding=False)
+    if os.environ.get("TJ_ATTN_STATIC") == "1":
+        plan = replace(plan, attn_dynamic=False)
     forced = os.environ.get("TJ_DELTA_DTYPE")
     if forced in _DTYPES:
         plan = replace(plan, delta_dtype=_DTYPES[forced])
