@@ -8,7 +8,10 @@
 //               in TMEM and commits stage/accumulator completion to mbarriers.
 //   warps 2..5  epilogue: tcgen05.ld the accumulator (one TMEM lane = one
 //               output row per thread), add bias, optional erf-GELU, convert,
-//               store; then hand the accumulator buffer back to the MMA warp.
+//               write 128-byte row pieces into a swizzled shared-memory tile
+//               (two per warp, alternating) that a TMA bulk store copies to
+//               C, so the global writes are whole lines; then hand the
+//               accumulator buffer back to the MMA warp.
 // The epilogue of tile i overlaps the main loop of tile i+1.  With a list of
 // live M tiles (padding-aware forward), only those row tiles are visited.  Output tiles are
 // visited in groups of 16 M-blocks so the CTAs resident at one time share
@@ -31,7 +34,10 @@ struct GemmCfg {
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators; 128/256/512
-  static constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + 256;
+  // Output staging: per epilogue warp two 32-row x 128-byte tiles.
+  static constexpr uint32_t kOutTile = 32 * 128;
+  static constexpr uint32_t kOutBytes = 4 * 2 * kOutTile;
+  static constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + kOutBytes + 256;
 };
 
 struct GemmArgs {
@@ -56,15 +62,13 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m_
   n_blk = r / gsize;
 }
 
-// Epilogue for one 32-column slice of one row: bias, activation, store.
-__device__ __forceinline__ void store_slice(const GemmArgs& a, int row, int col0,
-                                            const uint32_t (&acc)[32]) {
-  float v[32];
+// Bias and activation for one 32-column slice of one row.
+__device__ __forceinline__ void bias_act(const GemmArgs& a, int col0, const uint32_t (&acc)[32],
+                                         float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(acc[i]);
-  const bool full = col0 + 32 <= a.N;
   if (a.bias != nullptr) {
-    if (full) {
+    if (col0 + 32 <= a.N) {
       const float4* b4 = reinterpret_cast<const float4*>(a.bias + col0);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -84,35 +88,21 @@ __device__ __forceinline__ void store_slice(const GemmArgs& a, int row, int col0
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
   }
-  if (row >= a.M) return;
-  if (a.out_dtype == TJB_F32) {
-    float* dst = static_cast<float*>(a.C) + static_cast<int64_t>(row) * a.ldc + col0;
+}
+
+// One 128-byte row piece (8 x 16 bytes) into a 128-byte-swizzled staging
+// tile: 16-byte chunk k of row r lands at position k ^ (r & 7).
+__device__ __forceinline__ void stage_row(uint8_t* tile, int r, const uint32_t (&w)[32]) {
+  uint4* row = reinterpret_cast<uint4*>(tile + r * 128);
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (full || col0 + 4 * j < a.N)
-        reinterpret_cast<float4*>(dst)[j] =
-            make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-  } else {
-    uint32_t p[16];
-    if (a.out_dtype == TJB_BF16) {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) p[i] = Pack2<__nv_bfloat16>::pack(v[2 * i], v[2 * i + 1]);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) p[i] = Pack2<__half>::pack(v[2 * i], v[2 * i + 1]);
-    }
-    uint16_t* dst = static_cast<uint16_t*>(a.C) + static_cast<int64_t>(row) * a.ldc + col0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      if (full || col0 + 8 * j < a.N)
-        reinterpret_cast<uint4*>(dst)[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
-  }
+  for (int k = 0; k < 8; ++k)
+    row[k ^ (r & 7)] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
 }
 
 template <int BN>
 __global__ void __launch_bounds__(192, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const GemmArgs args) {
+                const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
   using Cfg = GemmCfg<BN>;
   constexpr int kStages = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -120,7 +110,8 @@ __global__ void __launch_bounds__(192, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages * Cfg::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + kStages * Cfg::kBBytes);
+  uint8_t* sOut = sB + kStages * Cfg::kBBytes;  // [epilogue warp][2][kOutTile]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + Cfg::kOutBytes);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
@@ -145,6 +136,7 @@ __global__ void __launch_bounds__(192, 1)
     fence_mbar_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    prefetch_tmap(&tmC);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
@@ -234,9 +226,8 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // -------------------------------------------------------------- epilogue
     const int quad = warp & 3;  // TMEM lanes this warp may access
-    const int r_in_tile = quad * 32 + lane;
     int acc = 0;
-    uint32_t acc_phase = 0;
+    uint32_t acc_phase = 0, n_out = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       int m_blk, n_blk;
       tile_coords(t, num_m, num_n, m_blk, n_blk);
@@ -245,16 +236,63 @@ __global__ void __launch_bounds__(192, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      const int row = m_blk * kBM + r_in_tile;
+      const int row0 = m_blk * kBM + quad * 32;
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      // One staged 32-row x 128-byte piece: wait until the store that last
+      // read this buffer is done, write it, hand it to TMA.
+      auto emit = [&](const uint32_t (&w)[32], int col) {
+        uint8_t* buf = sOut + (quad * 2 + (n_out & 1)) * Cfg::kOutTile;
+        if (lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+        stage_row(buf, lane, w);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, buf, col, row0);
+          bulk_commit();
+        }
+        ++n_out;
+      };
+      if (args.out_dtype == TJB_F32) {
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(taddr + c * 32, r);
-        tmem_ld_wait(r);
-        const int col0 = n_blk * BN + c * 32;
-        if (col0 < args.N) store_slice(args, row, col0, r);
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c * 32, r);
+          tmem_ld_wait(r);
+          const int col0 = n_blk * BN + c * 32;
+          if (col0 >= args.N) break;
+          float v[32];
+          bias_act(args, col0, r, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(v[i]);
+          emit(r, col0);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          const int col0 = n_blk * BN + c * 64;
+          uint32_t w[32];
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t r[32];
+            tmem_ld32(taddr + c * 64 + half * 32, r);
+            tmem_ld_wait(r);
+            float v[32];
+            bias_act(args, col0 + half * 32, r, v);
+            if (args.out_dtype == TJB_BF16) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                w[half * 16 + i] = Pack2<__nv_bfloat16>::pack(v[2 * i], v[2 * i + 1]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                w[half * 16 + i] = Pack2<__half>::pack(v[2 * i], v[2 * i + 1]);
+            }
+          }
+          if (col0 >= args.N) break;
+          emit(w, col0);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -264,6 +302,9 @@ __global__ void __launch_bounds__(192, 1)
         acc_phase ^= 1;
       }
     }
+    // Every bulk store has completed before the CTA exits.
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -305,10 +346,17 @@ int launch_gemm(const void* A, const void* B, const GemmArgs& args, int lda, int
   if (st != TJB_OK) return st;
   st = make_tmap_16bit(&tmB, 2, B, dimB, strB, boxB, bf16);
   if (st != TJB_OK) return st;
+  // Output: 128-byte boxes of 32 rows (32 fp32 or 64 16-bit columns).
+  const int esz = args.out_dtype == TJB_F32 ? 4 : 2;
+  CUtensorMap tmC;
+  st = make_tmap_2d(&tmC, args.out_dtype, args.C, static_cast<uint64_t>(args.N),
+                    static_cast<uint64_t>(args.M), static_cast<uint64_t>(args.ldc) * esz,
+                    static_cast<uint32_t>(128 / esz), 32);
+  if (st != TJB_OK) return st;
   const int num_tiles = ((args.M + kBM - 1) / kBM) * ((args.N + BN - 1) / BN);
   const int grid = num_tiles < num_sms() ? num_tiles : num_sms();
   return launch_kernel(gemm_kernel<BN>, dim3(grid), dim3(192), Cfg::kSmemBytes, stream, tmA, tmB,
-                    args);
+                       tmC, args);
 }
 
 }  // namespace

@@ -79,6 +79,23 @@ int make_tmap_16bit(CUtensorMap* map, int rank, const void* base, const uint64_t
   return r == CUDA_SUCCESS ? TJB_OK : TJB_ERR_TENSOR_MAP;
 }
 
+int make_tmap_2d(CUtensorMap* map, int dtype, const void* base, uint64_t cols, uint64_t rows,
+                 uint64_t ld_bytes, uint32_t box_cols, uint32_t box_rows) {
+  std::call_once(g_encode_once, load_encode);
+  if (g_encode == nullptr) return TJB_ERR_TENSOR_MAP;
+  const CUtensorMapDataType dt = dtype == TJB_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == TJB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t gdim[2] = {cols, rows};
+  cuuint64_t gstride[1] = {ld_bytes};
+  cuuint32_t bdim[2] = {box_cols, box_rows};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), gdim, gstride, bdim, estride,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TJB_OK : TJB_ERR_TENSOR_MAP;
+}
+
 // ------------------------------------------------------------ mask lengths
 // One CTA walks every row: lengths[b] = popcount of row b; a row is a prefix
 // mask iff it has no 0 -> 1 step.
