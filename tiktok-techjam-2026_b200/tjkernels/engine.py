@@ -12,7 +12,7 @@ Per layer (T = B*S tokens, residual stream fp32 [T, d]):
     res, h  = add_layernorm(res, pending, ln1)      # pending = last FFN delta
     qkv     = gemm(h, Wqkv) + bqkv                   # [T, 3d] -> [B,S,3,H,hd]
     ctx     = attention(qkv)                         # [T, d], causal, in place
-    attn    = gemm(ctx, Wo) + bo                     # delta (fp32 by default)
+    attn    = gemm(ctx, Wo) + bo                     # delta (compute dtype by default)
     res, h2 = add_layernorm(res, attn, ln2)
     pending = ffn(h2)                                # delta
     out     = add_layernorm(res, pending, final_ln)  # padded rows -> exact 0
@@ -149,6 +149,7 @@ class Engine:
         if res.dtype != torch.float32 or not res.is_contiguous():
             res = res.float().contiguous()
         own_res = res.data_ptr() != x.data_ptr()
+        delta_dtype = torch.float32 if plan.delta_dtype == torch.float32 else plan.compute_dtype
         pending: Optional[torch.Tensor] = None
         for lw in self.layers:
             res, h = K.fused_add_layernorm(
@@ -161,14 +162,14 @@ class Engine:
                                     causal=self.causal, lengths=lengths, key_mask=mask_u8,
                                     mask_flags=flags, scale=self.scale,
                                     sched=self._attn_sched if plan.attn_dynamic else None)
-            attn_out = K.gemm_bias(ctx, lw.wo, lw.bo, out_dtype=plan.delta_dtype, m_tiles=tiles)
+            attn_out = K.gemm_bias(ctx, lw.wo, lw.bo, out_dtype=delta_dtype, m_tiles=tiles)
             res, h2 = K.fused_add_layernorm(
                 res, attn_out, lw.ln2_w, lw.ln2_b, lw.ln2_eps, out_dtype=plan.compute_dtype,
                 residual_out=res if own_res else None, m_tiles=tiles)
             own_res = True
             ffn = K.ffn_single_kernel if (plan.ffn_single_kernel and
                                           K.ffn_fused_supports(d, self.ffn_dim)) else K.fused_ffn
-            pending = ffn(h2, lw.w1, lw.b1, lw.w2, lw.b2, out_dtype=plan.delta_dtype,
+            pending = ffn(h2, lw.w1, lw.b1, lw.w2, lw.b2, out_dtype=delta_dtype,
                           m_tiles=tiles)
 
         fw, fb, feps = self.final_ln
