@@ -190,6 +190,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();
+  griddep_launch_dependents();
   const bool prefix = args.lengths != nullptr &&
                       (args.mask_flags == nullptr || __ldg(args.mask_flags) == 0);
   const bool use_key_mask = args.key_mask != nullptr && !prefix;

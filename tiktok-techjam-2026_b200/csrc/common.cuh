@@ -40,6 +40,22 @@ __device__ __forceinline__ bool elect_one_lane() {
   return (threadIdx.x & 31) == 0;
 }
 
+// ----------------------------------------------- programmatic dependent launch
+// Kernels are launched so that the next kernel on the stream may start while
+// this one finishes.  Every kernel runs only its set-up (barrier init, tensor
+// memory allocation, descriptor prefetch) before griddep_wait(), which
+// returns once the previous kernel has completed and its writes are visible;
+// no global memory is read or written before it.  Each kernel then lets its
+// own successor launch: after its wait, so at most two grids overlap and the
+// successor can only occupy resources once every CTA of this grid is running.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // -------------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
@@ -584,9 +600,11 @@ inline int cuda_status(cudaError_t e) {
 
 inline int launch_status() { return cuda_status(cudaGetLastError()); }
 
-// cudaLaunchKernelEx wrapper returning a tjb_status.  (Programmatic
-// dependent launch was measured here: 3% slower on the forward, so plain
-// stream order is used.)
+// Programmatic dependent launch on (see griddep_wait); TJB_NO_PDL=1 in the
+// environment turns it off.
+bool pdl_enabled();
+
+// cudaLaunchKernelEx wrapper returning a tjb_status.
 template <typename... KArgs, typename... Args>
 inline int launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                          cudaStream_t stream, Args... args) {
@@ -595,6 +613,13 @@ inline int launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  if (pdl_enabled()) {
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
   return cuda_status(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
 }
 

@@ -118,6 +118,8 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
   tc_fence_after();
   cluster_sync();  // every CTA's barriers exist before any remote arrive
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();
+  griddep_launch_dependents();
   const uint32_t kOCol = 0, kG1Col = 256;
   const int num_m = args.m_tiles != nullptr ? __ldg(args.m_tiles) : (args.T + 127) / 128;
 

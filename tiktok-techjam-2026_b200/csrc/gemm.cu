@@ -146,6 +146,8 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();
+  griddep_launch_dependents();
   const int num_m = args.m_tiles != nullptr ? __ldg(args.m_tiles) : (args.M + kBM - 1) / kBM;
   const int num_n = (args.N + BN - 1) / BN;
   const int num_k = (args.K + kBK - 1) / kBK;

@@ -84,6 +84,8 @@ __global__ void __launch_bounds__(kBlock) add_layernorm_kernel(
   static_assert(TPR == 32 || TPR == 128 || TPR == 256, "threads per row");
   constexpr int kRowsPerBlock = kBlock / TPR;
   __shared__ float scratch[kBlock / 32];
+  griddep_wait();
+  griddep_launch_dependents();
 
   const int t = threadIdx.x % TPR;
   int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + threadIdx.x / TPR;

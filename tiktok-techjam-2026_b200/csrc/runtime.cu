@@ -2,6 +2,7 @@
 // status word, SM-count cache, tensor-map encoding through the driver entry
 // point (no link-time dependency on libcuda), and two small device kernels:
 // padding-mask classification and the bounded-wait self-test.
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -79,6 +80,14 @@ int make_tmap_16bit(CUtensorMap* map, int rank, const void* base, const uint64_t
   return r == CUDA_SUCCESS ? TJB_OK : TJB_ERR_TENSOR_MAP;
 }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("TJB_NO_PDL");
+    return !(e != nullptr && e[0] == '1');
+  }();
+  return on;
+}
+
 int make_tmap_2d(CUtensorMap* map, int dtype, const void* base, uint64_t cols, uint64_t rows,
                  uint64_t ld_bytes, uint32_t box_cols, uint32_t box_rows) {
   std::call_once(g_encode_once, load_encode);
@@ -105,6 +114,8 @@ __global__ void __launch_bounds__(1024) mask_lengths_kernel(const uint8_t* __res
                                                             int32_t* __restrict__ flags) {
   __shared__ int s_count[32];
   __shared__ int s_step[32];
+  griddep_wait();
+  griddep_launch_dependents();
   int any_step = 0;
   for (int b = 0; b < B; ++b) {
     const uint8_t* row = mask + static_cast<int64_t>(b) * S;
@@ -154,6 +165,8 @@ __global__ void __launch_bounds__(1024) row_tiles_kernel(const int32_t* __restri
                                                          int B, int S, int32_t* __restrict__ tiles) {
   __shared__ int s_warp[32];
   __shared__ int s_base;
+  griddep_wait();
+  griddep_launch_dependents();
   const int64_t T = static_cast<int64_t>(B) * S;
   const int n_tiles = static_cast<int>((T + 127) / 128);
   const bool all = lengths == nullptr || (flags != nullptr && __ldg(flags) != 0);
