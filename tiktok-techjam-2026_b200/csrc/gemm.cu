@@ -1,17 +1,19 @@
 // gemm.cu -- C = act(A * B^T + bias) on the 5th-generation tensor cores.
 //
-// Persistent, warp-specialised kernel, one CTA per SM (192 threads):
+// Persistent, warp-specialised kernel, one CTA per SM (320 threads):
 //   warp 0      TMA producer: streams 128x64 A tiles and BNx64 B tiles
 //               (128-byte swizzle) into a kStages-deep shared-memory ring.
 //   warp 1      allocates tensor memory; one lane issues tcgen05.mma
 //               (M=128, N=BN, K=16) into a double-buffered fp32 accumulator
 //               in TMEM and commits stage/accumulator completion to mbarriers.
-//   warps 2..5  epilogue: tcgen05.ld the accumulator (one TMEM lane = one
+//   warps 2..9  epilogue, two warps per TMEM lane quarter splitting the
+//               columns: tcgen05.ld the accumulator (one TMEM lane = one
 //               output row per thread), add bias, optional erf-GELU, convert,
 //               write 128-byte row pieces into a swizzled shared-memory tile
-//               (two per warp, alternating) that a TMA bulk store copies to
-//               C, so the global writes are whole lines; then hand the
-//               accumulator buffer back to the MMA warp.
+//               (one per warp) that a TMA bulk store copies to C, so the
+//               global writes are whole lines; then hand the accumulator
+//               buffer back to the MMA warp.  Eight warps rather than four:
+//               the GELU epilogue of the FFN's first GEMM is issue-bound.
 // The epilogue of tile i overlaps the main loop of tile i+1.  With a list of
 // live M tiles (padding-aware forward), only those row tiles are visited.  Output tiles are
 // visited in groups of 16 M-blocks so the CTAs resident at one time share
@@ -26,6 +28,7 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 x 16-bit = one 128-byte swizzle row
 constexpr int kGroupM = 16;
+constexpr int kGemmThreads = 320;
 
 template <int BN>
 struct GemmCfg {
@@ -34,9 +37,9 @@ struct GemmCfg {
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators; 128/256/512
-  // Output staging: per epilogue warp two 32-row x 128-byte tiles.
+  // Output staging: one 32-row x 128-byte tile per epilogue warp.
   static constexpr uint32_t kOutTile = 32 * 128;
-  static constexpr uint32_t kOutBytes = 4 * 2 * kOutTile;
+  static constexpr uint32_t kOutBytes = 8 * kOutTile;
   static constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + kOutBytes + 256;
 };
 
@@ -100,7 +103,7 @@ __device__ __forceinline__ void stage_row(uint8_t* tile, int r, const uint32_t (
 }
 
 template <int BN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
   using Cfg = GemmCfg<BN>;
@@ -110,7 +113,7 @@ __global__ void __launch_bounds__(192, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages * Cfg::kABytes;
-  uint8_t* sOut = sB + kStages * Cfg::kBBytes;  // [epilogue warp][2][kOutTile]
+  uint8_t* sOut = sB + kStages * Cfg::kBBytes;  // [epilogue warp][kOutTile]
   uint64_t* full = reinterpret_cast<uint64_t*>(sOut + Cfg::kOutBytes);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
@@ -129,7 +132,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], 8);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -227,9 +230,11 @@ __global__ void __launch_bounds__(192, 1)
     mbar_wait_drain(drain, 0);
   } else {
     // -------------------------------------------------------------- epilogue
-    const int quad = warp & 3;  // TMEM lanes this warp may access
+    const int quad = warp & 3;         // TMEM lanes this warp may access
+    const int half = (warp - 2) >> 2;  // which of the quarter's two warps
+    uint8_t* buf = sOut + (warp - 2) * Cfg::kOutTile;
     int acc = 0;
-    uint32_t acc_phase = 0, n_out = 0;
+    uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       int m_blk, n_blk;
       tile_coords(t, num_m, num_n, m_blk, n_blk);
@@ -244,8 +249,7 @@ __global__ void __launch_bounds__(192, 1)
       // One staged 32-row x 128-byte piece: wait until the store that last
       // read this buffer is done, write it, hand it to TMA.
       auto emit = [&](const uint32_t (&w)[32], int col) {
-        uint8_t* buf = sOut + (quad * 2 + (n_out & 1)) * Cfg::kOutTile;
-        if (lane == 0) bulk_wait_read<1>();
+        if (lane == 0) bulk_wait_read<0>();
         __syncwarp();
         stage_row(buf, lane, w);
         fence_proxy_async_smem();
@@ -254,11 +258,10 @@ __global__ void __launch_bounds__(192, 1)
           tma_store_2d(&tmC, buf, col, row0);
           bulk_commit();
         }
-        ++n_out;
       };
       if (args.out_dtype == TJB_F32) {
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half; c < BN / 32; c += 2) {
           uint32_t r[32];
           tmem_ld32(taddr + c * 32, r);
           tmem_ld_wait(r);
@@ -272,7 +275,7 @@ __global__ void __launch_bounds__(192, 1)
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
+        for (int c = half; c < BN / 64; c += 2) {
           const int col0 = n_blk * BN + c * 64;
           uint32_t w[32];
 #pragma unroll
@@ -357,8 +360,8 @@ int launch_gemm(const void* A, const void* B, const GemmArgs& args, int lda, int
   if (st != TJB_OK) return st;
   const int num_tiles = ((args.M + kBM - 1) / kBM) * ((args.N + BN - 1) / BN);
   const int grid = num_tiles < num_sms() ? num_tiles : num_sms();
-  return launch_kernel(gemm_kernel<BN>, dim3(grid), dim3(192), Cfg::kSmemBytes, stream, tmA, tmB,
-                       tmC, args);
+  return launch_kernel(gemm_kernel<BN>, dim3(grid), dim3(kGemmThreads), Cfg::kSmemBytes, stream,
+                       tmA, tmB, tmC, args);
 }
 
 }  // namespace
