@@ -64,7 +64,8 @@ __device__ __forceinline__ float fast_exp2(float x) {
 // O is rescaled lazily: only when a row's max grows by more than 2^8 (P stays
 // below 256 in 16-bit, every sum stays in fp32 range); O / l is exact for any
 // choice of the reference max.
-constexpr int kPairThreads = 320;
+constexpr int kPairThreads = 352;
+constexpr int kMmaWarp1 = kPairThreads / 32 - 1;  // issues group 1's MMAs (warp 1: group 0's)
 constexpr int kItemSlots = 4;  // work items queued from the producer to the other warps
 constexpr float kRescaleLog2 = 8.0f;
 
@@ -128,6 +129,59 @@ __device__ __forceinline__ PairItem decode_pair(int w, const AttnArgs& a, int nu
   return it;
 }
 
+// Warp-collective bounded wait: every lane agrees on the outcome.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort));
+}
+
+// S = Q K^T into TMEM columns d_s: HD/16 K-steps over 64-column sub-tiles.
+template <int HD>
+__device__ __forceinline__ void issue_qk(uint32_t d_s, uint32_t qa, uint32_t ka, uint32_t idesc) {
+#pragma unroll
+  for (int k = 0; k < HD / 16; ++k) {
+    const uint32_t off = (k >> 2) * kSub + (k & 3) * 32;
+    umma_ss_w(d_s, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(ka + off, 16, 1024), idesc,
+              k > 0 ? 1u : 0u);
+  }
+}
+
+// O (+)= P V: P read from TMEM columns pa, V (MN-major) from shared memory.
+template <int HD>
+__device__ __forceinline__ void issue_pv(uint32_t d_o, uint32_t pa, uint32_t va, uint32_t idesc,
+                                         bool accumulate) {
+#pragma unroll
+  for (int k = 0; k < kTileK / 16; ++k)
+    umma_ts_w(d_o, pa + k * 8, sdesc_sw128(va + k * 2048, kSub, 1024), idesc,
+              (accumulate || k > 0) ? 1u : 0u);
+}
+
+// One group's S = Q K^T (the K tile has landed): with separate P columns,
+// wait for the softmax to hold the previous scores (s_free); issue, commit.
+template <int HD>
+__device__ __forceinline__ bool qk_step(uint64_t* s_free, uint64_t* s_full, uint32_t& sc,
+                                        volatile int* abort, uint32_t d_s, uint32_t q_addr,
+                                        uint32_t k_addr, uint32_t idesc) {
+  if (s_free != nullptr && sc > 0 && !warp_wait(s_free, (sc - 1) & 1, abort)) return false;
+  tc_fence_after();
+  issue_qk<HD>(d_s, q_addr, k_addr, idesc);
+  umma_commit_w(s_full);
+  ++sc;
+  return true;
+}
+
+// One group's O += P V (the V tile has landed): wait for P, issue, commit.
+template <int HD>
+__device__ __forceinline__ bool pv_step(uint64_t* p_full, uint64_t* pv_done, uint32_t& pvc,
+                                        volatile int* abort, uint32_t d_o, uint32_t pa,
+                                        uint32_t v_addr, uint32_t idesc, bool accumulate) {
+  if (!warp_wait(p_full, pvc & 1, abort)) return false;
+  tc_fence_after();
+  issue_pv<HD>(d_o, pa, v_addr, idesc, accumulate);
+  umma_commit_w(pv_done);
+  ++pvc;
+  return true;
+}
+
 template <int HD, bool kBF16>
 __global__ void __launch_bounds__(kPairThreads, 1)
     attn_pair_kernel(const __grid_constant__ CUtensorMap tm, const AttnArgs args) {
@@ -148,8 +202,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint64_t* s_free = s_full + 2;          // [group]
   uint64_t* p_full = s_free + 2;          // [group]
   uint64_t* pv_done = p_full + 2;         // [group]
-  uint64_t* drain = pv_done + 2;
-  uint64_t* item_full = drain + 1;                 // [kItemSlots]
+  uint64_t* drain = pv_done + 2;                   // [issuer]
+  uint64_t* item_full = drain + 2;                 // [kItemSlots]
   uint64_t* item_empty = item_full + kItemSlots;   // [kItemSlots]
   volatile int* item_q = reinterpret_cast<volatile int*>(item_empty + kItemSlots);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_empty + kItemSlots) + kItemSlots;
@@ -163,7 +217,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
+      mbar_init(&q_empty[i], 2);  // one commit per MMA issuer
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 4);
       mbar_init(&p_full[i], 4);
@@ -171,12 +225,13 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     }
     for (uint32_t s = 0; s < kSlots; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&kv_empty[s], 2);
     }
-    mbar_init(drain, 1);
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     for (int i = 0; i < kItemSlots; ++i) {
       mbar_init(&item_full[i], 1);
-      mbar_init(&item_empty[i], 1 + 8);  // the MMA warp and the eight softmax warps
+      mbar_init(&item_empty[i], 2 + 8);  // the two MMA warps and the eight softmax warps
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -254,110 +309,88 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       for (uint32_t k = seq >= kSlots ? seq - kSlots : 0; k < seq; ++k)
         mbar_wait_drain(&kv_full[k % kSlots], (k / kSlots) & 1);
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    // The whole warp runs this loop, converged; one elected lane issues.
+  } else if (warp == 1 || warp == kMmaWarp1) {
+    // ----------------------------------------------------------- MMA issuers
+    // One warp per query-tile group (warp 1: group 0, the last warp: group
+    // 1), on different SM sub-partitions: a lone issuer sharing its
+    // sub-partition with two busy softmax warps measured ~100 clocks per MMA
+    // against the tensor pipe's 64.  Each warp runs converged and one elected
+    // lane issues; its commits track only its own group's MMAs, and every
+    // shared slot (K/V tile, Q pair, work item) counts one release from each.
+    const int g = warp == 1 ? 0 : 1;
     const uint32_t q_base = smem_u32(sQ);
+    const uint32_t d_s = tmem_base + g * kTileK;
+    const uint32_t d_o = tmem_base + Cfg::kOCol + g * HD;
+    const uint32_t pa = tmem_base + Cfg::kPCol + g * Cfg::kPStride;
     uint32_t n_items = 0, base = 0;  // base: ring sequence number of the item's K(0)
-    uint32_t sc[2] = {0, 0}, pvc[2] = {0, 0};
+    uint32_t sc = 0, pvc = 0;        // this group's QK / PV tiles issued
     bool ok = true;
-    auto wait = [&](uint64_t* bar, uint32_t parity) {
-      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
-    };
     for (uint32_t qn = 0; ok; ++qn) {
       const uint32_t islot = qn % kItemSlots;
-      if (!wait(&item_full[islot], (qn / kItemSlots) & 1)) break;
-      const int w = item_q[islot];
+      if (!warp_wait(&item_full[islot], (qn / kItemSlots) & 1, abort_flag)) break;
+      const int w = __shfl_sync(0xffffffffu, item_q[islot], 0);
       __syncwarp();
       if (lane == 0) mbar_arrive(&item_empty[islot]);
       if (w < 0) break;
       const PairItem it = decode_pair(w, args, num_pairs, prefix);
       const int n = max(it.n_kv[0], it.n_kv[1]);
       if (n == 0) continue;
+      const int ng = it.n_kv[g];
       const uint32_t slot = n_items % kQSlots;
-      if (!wait(&q_full[slot], (n_items / kQSlots) & 1)) break;
+      if (!warp_wait(&q_full[slot], (n_items / kQSlots) & 1, abort_flag)) break;
       ++n_items;
-      const uint32_t q_addr = q_base + slot * 2 * Cfg::kQBytes;
-      for (int j = 0; j <= n && ok; ++j) {
+      const uint32_t q_addr = q_base + (slot * 2 + g) * Cfg::kQBytes;
+      for (int j = 0; j <= n; ++j) {
         const uint32_t kseq = base + 2 * j, vseq = kseq - 1;  // K(j), V(j-1)
         const uint32_t kslot = kseq % kSlots, vslot = vseq % kSlots;
+        const bool do_pv = j >= 1 && j - 1 < ng;
+        const bool do_qk = j < ng;
         const uint32_t k_addr = smem_u32(sKV + kslot * Cfg::kTileBytes);
         const uint32_t v_addr = smem_u32(sKV + vslot * Cfg::kTileBytes);
-        bool k_ready = j >= n, v_ready = j == 0;
-        // S_g = Q_g K_j^T (HD/16 K-steps over kSubs 64-column sub-tiles).
-        auto issue_qk = [&](int g) {
-          if (!k_ready) {
-            if (!wait(&kv_full[kslot], (kseq / kSlots) & 1)) return false;
-            tc_fence_after();
-            k_ready = true;
+        // Each issuer waits for every K/V tile it releases, used by its
+        // group or not, so that its release of a slot can never run ahead of
+        // the fill it belongs to (the slot's barrier counts both issuers).
+        const bool has_k = j < n, has_v = j >= 1;
+        bool good = true;
+        auto v_phase = [&]() {
+          if (has_v) {
+            good = warp_wait(&kv_full[vslot], (vseq / kSlots) & 1, abort_flag);
+            if (good && do_pv)
+              good = pv_step<HD>(&p_full[g], &pv_done[g], pvc, abort_flag, d_o, pa, v_addr,
+                                 args.idesc_pv, j > 1);
+            if (good) umma_commit_w(&kv_empty[vslot]);
           }
-          const uint32_t qa = q_addr + g * Cfg::kQBytes;
-          const uint32_t d_s = tmem_base + static_cast<uint32_t>(g * kTileK);
-#pragma unroll
-          for (int k = 0; k < HD / 16; ++k) {
-            const uint32_t off = (k >> 2) * kSub + (k & 3) * 32;
-            umma_ss_w(d_s, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(k_addr + off, 16, 1024),
-                    args.idesc_qk, k > 0 ? 1u : 0u);
-          }
-          umma_commit_w(&s_full[g]);
-          ++sc[g];
-          return true;
         };
-        // O_g += P_g V_{j-1}, P_g read from tensor memory.
-        auto issue_pv = [&](int g, int jp) {
-          if (!v_ready) {
-            if (!wait(&kv_full[vslot], (vseq / kSlots) & 1)) return false;
-            v_ready = true;
+        auto k_phase = [&]() {
+          if (has_k && good) {
+            good = warp_wait(&kv_full[kslot], (kseq / kSlots) & 1, abort_flag);
+            if (good && do_qk)
+              good = qk_step<HD>(Cfg::kAlias ? nullptr : &s_free[g], &s_full[g], sc, abort_flag,
+                                 d_s, q_addr, k_addr, args.idesc_qk);
+            if (good) umma_commit_w(&kv_empty[kslot]);
           }
-          if (!wait(&p_full[g], pvc[g] & 1)) return false;
-          tc_fence_after();
-          const uint32_t pa = tmem_base + Cfg::kPCol + g * Cfg::kPStride;
-          const uint32_t d_o = tmem_base + Cfg::kOCol + g * HD;
-#pragma unroll
-          for (int k = 0; k < kTileK / 16; ++k)
-            umma_ts_w(d_o, pa + k * 8, sdesc_sw128(v_addr + k * 2048, kSub, 1024),
-                    args.idesc_pv, (jp > 0 || k > 0) ? 1u : 0u);
-          umma_commit_w(&pv_done[g]);
-          ++pvc[g];
-          return true;
         };
         if constexpr (Cfg::kAlias) {
-          // Per group: PV of tile j-1 (reads P out of the score columns),
-          // then QK of tile j into the same columns.  V(j-1) is released
-          // once both PVs are issued, K(j) once both QKs are.
-#pragma unroll
-          for (int g = 0; g < 2; ++g) {
-            if (ok && j >= 1 && j - 1 < it.n_kv[g]) ok = issue_pv(g, j - 1);
-            if (ok && g == 1 && j >= 1) umma_commit_w(&kv_empty[vslot]);
-            if (ok && j < it.n_kv[g]) ok = issue_qk(g);
-          }
-          if (ok && j < n) umma_commit_w(&kv_empty[kslot]);
+          // PV of tile j-1 (reads P out of the score columns), then QK of
+          // tile j into the same columns; the tensor pipe keeps this order.
+          v_phase();
+          k_phase();
         } else {
-          // Scores first (S_g is released as soon as it is in registers),
-          // then PV of the previous tile from the separate P columns.
-#pragma unroll
-          for (int g = 0; g < 2; ++g) {
-            if (!ok || j >= it.n_kv[g]) continue;
-            if (sc[g] > 0 && !wait(&s_free[g], (sc[g] - 1) & 1)) {
-              ok = false;
-              continue;
-            }
-            tc_fence_after();
-            ok = issue_qk(g);
-          }
-          if (ok && j < n) umma_commit_w(&kv_empty[kslot]);
-#pragma unroll
-          for (int g = 0; g < 2; ++g)
-            if (ok && j >= 1 && j - 1 < it.n_kv[g]) ok = issue_pv(g, j - 1);
-          if (ok && j >= 1) umma_commit_w(&kv_empty[vslot]);
+          // Scores first (S is released as soon as the softmax holds it in
+          // registers), then PV of the previous tile from the P columns.
+          k_phase();
+          if (good) v_phase();
         }
-        if (!ok) break;
+        if (!good) {
+          ok = false;
+          break;
+        }
         if (j == n - 1) umma_commit_w(&q_empty[slot]);
       }
       base += 2 * n;
     }
-    umma_commit_w(drain);
-    mbar_wait_drain(drain, 0);
+    umma_commit_w(&drain[g]);
+    mbar_wait_drain(&drain[g], 0);
   } else {
     // -------------------------------------------------------------- softmax
     const int g = (warp - 2) >> 2;  // group 0: warps 2-5, group 1: warps 6-9
