@@ -395,14 +395,21 @@ extern "C" int tjb_gemm_bias_tiles(const void* A, const void* B, const float* bi
   args.act = act;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int sms = num_sms();
-  const int mt = (M + kBM - 1) / kBM;
-  const long tiles256 = static_cast<long>(mt) * ((N + 255) / 256);
-  const long tiles128 = static_cast<long>(mt) * ((N + 127) / 128);
-  if (N >= 256 && tiles256 >= sms) {
+  // Tile width: the fewest waves weighted by each width's time per tile
+  // relative to a 256-wide one (fitted to a B200 sweep of M 4608-15104,
+  // N 1024-4096, K 1024-4096: 0.65 for 128-wide, 0.5 for 64-wide).  With a
+  // live-tile list the listed count is not known on the host, so M is taken
+  // as given.
+  const long mt = (M + kBM - 1) / kBM;
+  auto waves = [&](int bn) { return (mt * ((N + bn - 1) / bn) + sms - 1) / sms; };
+  const double c256 = N >= 256 ? static_cast<double>(waves(256)) : 1e30;
+  const double c128 = N >= 128 ? waves(128) * 0.65 : 1e30;
+  const double c64 = waves(64) * 0.5;
+  if (c256 <= c128 && c256 <= c64) {
     args.idesc = idesc_f16(kBM, 256, bf16, false);
     return launch_gemm<256>(A, B, args, lda, ldb, bf16, s);
   }
-  if (N >= 128 && tiles128 >= sms / 2) {
+  if (c128 <= c64) {
     args.idesc = idesc_f16(kBM, 128, bf16, false);
     return launch_gemm<128>(A, B, args, lda, ldb, bf16, s);
   }
