@@ -4,11 +4,13 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl tjb|reference]
 
 Workload (``--config``, default 2): the BASELINE configs of the fused causal
-encoder forward.  Each GPU runs the full config's batch (weak scaling: the
+encoder forward.  Each GPU runs a full config-sized batch (weak scaling: the
 per-GPU work is fixed and N GPUs process N times the sequences, with no
-collective in the forward; sequences are independent).  Inputs are seeded
-synthetic tensors with the harness's shapes and padding distribution
-(``generate_random_case``), weights the harness's default initialisation.
+collective in the forward; sequences are independent): every rank gets the
+same seeded set of prefix lengths (its own data), so the per-GPU work is the
+same at every N.  Inputs are synthetic tensors with the harness's shapes and
+padding distribution (``generate_random_case``), weights the harness's
+default initialisation.
 
 One step = one ``model(x, mask)`` call through the harness hook (the engine,
 CUDA-graph replay included), exactly what the reference harness times.
@@ -63,16 +65,26 @@ METRIC = "forward tokens/sec"
 FLUSH_BYTES = 256 << 20
 
 
-def synthetic_case(b, s, d, seed, padding):
-    """Seeded x ~ N(0,1) and prefix mask with lengths uniform in
-    [max(1, round(S(1-p))), S] (the harness's generate_random_case)."""
+def synthetic_case(b, s, d, seed, padding, rank=0, world=1):
+    """This rank's batch: b sequences with prefix lengths uniform in
+    [max(1, round(S(1-p))), S] (the harness's generate_random_case), drawn
+    once from ``seed`` and the same on every rank, so that each GPU does the
+    same work at any N (weak scaling measures the system, not the draw);
+    x ~ N(0,1) per sequence, seeded by its global index rank*b + i, zero on
+    padded rows."""
     gen = torch.Generator(device="cpu")
     gen.manual_seed(seed)
-    x = torch.randn(b, s, d, generator=gen, dtype=torch.float32)
     if padding <= 0:
-        return x, torch.ones(b, s, dtype=torch.bool)
-    min_valid = max(1, int(round(s * (1.0 - padding))))
-    lengths = torch.randint(low=min_valid, high=s + 1, size=(b,), generator=gen)
+        lengths = torch.full((b,), s, dtype=torch.long)
+    else:
+        min_valid = max(1, int(round(s * (1.0 - padding))))
+        lengths = torch.randint(low=min_valid, high=s + 1, size=(b,), generator=gen)
+    xs = []
+    for i in range(b):
+        g = torch.Generator(device="cpu")
+        g.manual_seed(seed + 1 + rank * b + i)
+        xs.append(torch.randn(s, d, generator=g, dtype=torch.float32))
+    x = torch.stack(xs)
     mask = torch.arange(s)[None, :] < lengths[:, None]
     return x.masked_fill(~mask[..., None], 0), mask
 
@@ -347,7 +359,7 @@ def main():
     cfg = EncoderConfig(b, s, d, h, f, layers, True)
     torch.manual_seed(0)
     model = Encoder(cfg).to(dev).eval()
-    x_cpu, mask_cpu = synthetic_case(b, s, d, 100000 + rank, pad)
+    x_cpu, mask_cpu = synthetic_case(b, s, d, 100000, pad, rank, world)
     x, mask = x_cpu.to(dev), mask_cpu.to(dev)
     lengths = mask_cpu.sum(-1).tolist()
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)

@@ -111,3 +111,18 @@ def test_survivor_raises_when_a_rank_dies(tmp_path):
         outcome = f.read()
     assert outcome.startswith("raised"), outcome
     assert float(outcome.split()[2].rstrip("s:")) < 30.0
+
+
+def test_balanced_equal_shards():
+    from tjkernels.parallel import balanced_equal_shards
+    import random
+    rng = random.Random(7)
+    for world in (1, 2, 4, 8):
+        lengths = [rng.randint(1024, 2048) for _ in range(8 * world)]
+        shards = balanced_equal_shards(lengths, world)
+        assert sorted(i for sh in shards for i in sh) == list(range(len(lengths)))
+        assert all(len(sh) == 8 for sh in shards)
+        work = [sum(lengths[i] * (lengths[i] + 1) / 2 for i in sh) for sh in shards]
+        assert max(work) / min(work) < 1.15
+    with pytest.raises(ValueError):
+        balanced_equal_shards([1, 2, 3], 2)

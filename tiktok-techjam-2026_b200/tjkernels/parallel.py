@@ -37,3 +37,18 @@ def balanced_shards(lengths: Sequence[int], world: int) -> List[List[int]]:
         shards[r].append(i)
         loads[r] += n * (n + 1) / 2 + n
     return [sorted(s) for s in shards]
+
+
+def balanced_equal_shards(lengths: Sequence[int], world: int) -> List[List[int]]:
+    """Like ``balanced_shards`` but every rank gets the same number of
+    sequences (``len(lengths)`` must be a multiple of ``world``): sort by
+    causal work, longest first, and deal in snake order (0..w-1, w-1..0, ...),
+    so each rank's batch has the same shape and close to the same work."""
+    if world <= 0 or len(lengths) % world != 0:
+        raise ValueError("the number of sequences must be a positive multiple of world")
+    order = sorted(range(len(lengths)), key=lambda i: (-int(lengths[i]), i))
+    shards: List[List[int]] = [[] for _ in range(world)]
+    for k, i in enumerate(order):
+        rnd, pos = divmod(k, world)
+        shards[pos if rnd % 2 == 0 else world - 1 - pos].append(i)
+    return [sorted(s) for s in shards]
