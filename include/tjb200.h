@@ -27,6 +27,7 @@
 #ifndef TJB200_H
 #define TJB200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -114,6 +115,28 @@ int tjb_gemm_bias_tiles(const void* A, const void* B, const float* bias, void* C
                         tjb_stream_t stream);
 
 /*
+ * Bytes of device workspace tjb_gemm_bias_tiles_ws / tjb_ffn_tiles_ws need
+ * (about 21 MB).
+ */
+size_t tjb_gemm_workspace_bytes(void);
+
+/*
+ * tjb_gemm_bias_tiles with a split-K tail: when the output tiles do not fill
+ * a whole number of waves over the SMs, each tile of the last partial wave
+ * is split along K over CTAs that would otherwise idle, the partial sums
+ * meeting in the workspace (fp32).  workspace: tjb_gemm_workspace_bytes()
+ * bytes of device memory, 16-byte aligned, zero-filled before its first use;
+ * each call leaves it ready for the next.  Calls that may run at the same
+ * time need separate workspaces.  Same result layout as
+ * tjb_gemm_bias_tiles; the summation order of the split tiles differs (fp32).
+ * No counterpart in the reference (torch.addmm).
+ */
+int tjb_gemm_bias_tiles_ws(const void* A, const void* B, const float* bias, void* C,
+                           int M, int N, int K, int lda, int ldb, int ldc,
+                           int in_dtype, int out_dtype, int act, const int32_t* m_tiles,
+                           void* workspace, size_t workspace_bytes, tjb_stream_t stream);
+
+/*
  * Causal (or full) multi-head attention forward on tcgen05 tensor cores,
  * reading Q, K and V in place from the packed QKV projection output.
  *   qkv: [B, S, 3, H, hd] in dtype (f16 or bf16), row pitch 3*H*hd
@@ -166,6 +189,13 @@ int tjb_ffn(const void* h, const void* w1, const float* b1, const void* w2,
 int tjb_ffn_tiles(const void* h, const void* w1, const float* b1, const void* w2,
                   const float* b2, void* out, void* hidden, int T, int d, int F,
                   int in_dtype, int out_dtype, const int32_t* m_tiles, tjb_stream_t stream);
+
+/* tjb_ffn_tiles whose two GEMMs use the split-K tail (see
+ * tjb_gemm_bias_tiles_ws; one workspace serves both, they run in order). */
+int tjb_ffn_tiles_ws(const void* h, const void* w1, const float* b1, const void* w2,
+                     const float* b2, void* out, void* hidden, int T, int d, int F,
+                     int in_dtype, int out_dtype, const int32_t* m_tiles, void* workspace,
+                     size_t workspace_bytes, tjb_stream_t stream);
 
 /*
  * The feed-forward block as ONE kernel whose [T, F] hidden activations never

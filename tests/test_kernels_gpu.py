@@ -89,6 +89,52 @@ def test_gemm_bias(m, n, k, dtype):
     assert ((out16.double() - ref).abs() <= tol * ref.abs() + 1e-3 * scale).all()
 
 
+SPLIT_SHAPES = [(5120, 1024, 1024), (5120, 1024, 4096), (4608, 3072, 1024), (300, 136, 512),
+                (2000, 1032, 2048), (129, 64, 64)]
+
+
+@pytest.mark.parametrize("m,n,k", SPLIT_SHAPES)
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16])
+def test_gemm_split_tail(m, n, k, out_dtype):
+    """The split-K tail (last partial wave of tiles split along K over idle
+    SMs, partials meeting in the workspace) matches fp64 and the whole-tile
+    kernel, with GELU and a live-tile list too, and leaves the workspace's
+    counters at zero for the next call."""
+    g = torch.Generator(device=DEV).manual_seed(m * 7 + n + k)
+    a = torch.randn(m, k, device=DEV, generator=g).half()
+    w = (torch.randn(n, k, device=DEV, generator=g) / math.sqrt(k)).half()
+    bias = torch.randn(n, device=DEV, generator=g)
+    ws = K().gemm_workspace(DEV)
+    flags_at = ws.numel() - 256 * 4
+    for act in (K().ACT_NONE, K().ACT_GELU):
+        ref = a.double() @ w.double().T + bias.double()
+        if act == K().ACT_GELU:
+            ref = F.gelu(ref, approximate="none")
+        for _ in range(2):
+            got = K().gemm_bias(a, w, bias, act=act, out_dtype=out_dtype, workspace=ws)
+            whole = K().gemm_bias(a, w, bias, act=act, out_dtype=out_dtype)
+            scale = ref.abs().max().item() + 1e-6
+            tol = 1e-5 if out_dtype == torch.float32 else 2 ** -10
+            assert ((got.double() - ref).abs() <= tol * ref.abs() + 1e-4 * scale).all()
+            assert (got.double() - whole.double()).abs().max().item() <= 2e-3 * scale
+            assert int(ws[flags_at:].view(torch.int32).abs().sum()) == 0
+    # Live-tile list: every other 128-row tile.
+    n_tiles = (m + 127) // 128
+    live = list(range(0, n_tiles, 2))
+    tiles = torch.tensor([len(live)] + live + [0] * (n_tiles - len(live)), dtype=torch.int32,
+                         device=DEV)
+    out = torch.zeros(m, n, dtype=out_dtype, device=DEV)
+    K().gemm_bias(a, w, bias, out_dtype=out_dtype, out=out, m_tiles=tiles, workspace=ws)
+    ref = a.double() @ w.double().T + bias.double()
+    rows = torch.zeros(m, dtype=torch.bool, device=DEV)
+    for t in live:
+        rows[t * 128:(t + 1) * 128] = True
+    scale = ref.abs().max().item() + 1e-6
+    assert ((out.double()[rows] - ref[rows]).abs() <= 2 ** -10 * ref[rows].abs() + 1e-4 * scale).all()
+    assert bool((out[~rows] == 0).all())
+    assert int(ws[flags_at:].view(torch.int32).abs().sum()) == 0
+
+
 @pytest.mark.parametrize("m,n,k", [(200, 512, 256), (1024, 4096, 1024)])
 def test_gemm_gelu(m, n, k):
     a = torch.randn(m, k, device=DEV).bfloat16()

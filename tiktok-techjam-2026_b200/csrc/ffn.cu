@@ -20,6 +20,19 @@ extern "C" int tjb_ffn_tiles(const void* h, const void* w1, const float* b1, con
                              m_tiles, stream);
 }
 
+extern "C" int tjb_ffn_tiles_ws(const void* h, const void* w1, const float* b1, const void* w2,
+                                const float* b2, void* out, void* hidden, int T, int d, int F,
+                                int in_dtype, int out_dtype, const int32_t* m_tiles,
+                                void* workspace, size_t workspace_bytes, tjb_stream_t stream) {
+  if (!h || !w1 || !w2 || !out || !hidden || !workspace || T < 0 || d <= 0 || F <= 0)
+    return TJB_ERR_INVALID_ARGUMENT;
+  int st = tjb_gemm_bias_tiles_ws(h, w1, b1, hidden, T, F, d, d, d, F, in_dtype, in_dtype, 1,
+                                  m_tiles, workspace, workspace_bytes, stream);
+  if (st != TJB_OK) return st;
+  return tjb_gemm_bias_tiles_ws(hidden, w2, b2, out, T, d, F, F, F, d, in_dtype, out_dtype, 0,
+                                m_tiles, workspace, workspace_bytes, stream);
+}
+
 extern "C" int tjb_ffn(const void* h, const void* w1, const float* b1, const void* w2,
                        const float* b2, void* out, void* hidden, int T, int d, int F,
                        int in_dtype, int out_dtype, tjb_stream_t stream) {

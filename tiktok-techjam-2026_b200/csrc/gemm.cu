@@ -53,7 +53,58 @@ struct GemmArgs {
   int out_dtype;
   int act;
   uint32_t idesc;
+  // Split-K tail workspace (null: every tile is computed whole by one CTA).
+  float* ws;      // [kSkMaxPartials][kBM][256] fp32 partial tiles
+  int* ws_flags;  // [kSkMaxPartials] arrival counts, zero between launches
 };
+
+// Split-K tail.  When the tiles do not fill a whole number of waves over the
+// grid, the leftover tiles of the last wave are each split along K over
+// `splits` CTAs that would otherwise idle: the CTA holding k-split 0 owns the
+// tile, the others write fp32 partials into the workspace and count in
+// ws_flags; the owner adds them before its epilogue and returns the count to
+// zero.  A work unit is a whole tile (the first dp_tiles) or one k-split.
+constexpr int kSkMaxSplits = 8;
+constexpr int kSkMaxPartials = 160;  // >= grid - leftover tiles
+constexpr size_t kSkPartialBytes = static_cast<size_t>(kSkMaxPartials) * kBM * 256 * 4;
+
+struct GemmUnit {
+  int tile, split, kb0, kb1;
+};
+
+__device__ __forceinline__ GemmUnit gemm_unit(int u, int dp_tiles, int splits, int num_k) {
+  GemmUnit x;
+  if (u < dp_tiles) {
+    x.tile = u;
+    x.split = 0;
+    x.kb0 = 0;
+    x.kb1 = num_k;
+    return x;
+  }
+  const int l = u - dp_tiles;
+  x.tile = dp_tiles + l / splits;
+  x.split = l % splits;
+  x.kb0 = x.split * num_k / splits;
+  x.kb1 = (x.split + 1) * num_k / splits;
+  return x;
+}
+
+// Bounded wait until *count reaches target (acquire).
+__device__ __forceinline__ bool wait_count(const int* count, int target, volatile int* abort) {
+  const uint64_t t0 = globaltimer();
+  for (;;) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(count) : "memory");
+    if (v >= target) return true;
+    if (*abort) return false;
+    if (globaltimer() - t0 > kWaitTimeoutNs) {
+      *abort = 1;
+      record_status(TJB_ERR_DEVICE_TIMEOUT);
+      return false;
+    }
+    __nanosleep(100);
+  }
+}
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m_blk, int& n_blk) {
   const int per_group = kGroupM * num_n;
@@ -155,6 +206,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int num_n = (args.N + BN - 1) / BN;
   const int num_k = (args.K + kBK - 1) / kBK;
   const int num_tiles = num_m * num_n;
+  int dp_tiles = num_tiles, splits = 1;
+  if (args.ws != nullptr) {
+    const int grid = static_cast<int>(gridDim.x);
+    const int rem = num_tiles % grid;
+    if (rem > 0) {
+      const int sk = min(min(grid / rem, kSkMaxSplits), num_k / 2);
+      if (sk >= 2) {
+        dp_tiles = num_tiles - rem;
+        splits = sk;
+      }
+    }
+  }
+  const int num_units = dp_tiles + (num_tiles - dp_tiles) * splits;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -162,11 +226,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0, issued = 0, issued_parity = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const GemmUnit un = gemm_unit(u, dp_tiles, splits, num_k);
         int m_blk, n_blk;
-        tile_coords(t, num_m, num_n, m_blk, n_blk);
+        tile_coords(un.tile, num_m, num_n, m_blk, n_blk);
         if (args.m_tiles != nullptr) m_blk = __ldg(args.m_tiles + 1 + m_blk);
-        for (int kb = 0; kb < num_k; ++kb) {
+        for (int kb = un.kb0; kb < un.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
             ok = false;
             break;
@@ -195,11 +260,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     auto wait = [&](uint64_t* bar, uint32_t parity) {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
     };
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+    for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+      const GemmUnit un = gemm_unit(u, dp_tiles, splits, num_k);
       if (!wait(&tempty[acc], acc_phase ^ 1)) break;
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-      for (int kb = 0; kb < num_k; ++kb) {
+      for (int kb = un.kb0; kb < un.kb1; ++kb) {
         if (!wait(&full[stage], phase)) {
           ok = false;
           break;
@@ -210,7 +276,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
         for (int k = 0; k < kBK / 16; ++k) {
           umma_ss_w(d_tmem, sdesc_sw128(a0 + k * 32, 16, 1024),
-                    sdesc_sw128(b0 + k * 32, 16, 1024), args.idesc, (kb | k) != 0 ? 1u : 0u);
+                    sdesc_sw128(b0 + k * 32, 16, 1024), args.idesc,
+                    (kb > un.kb0 || k > 0) ? 1u : 0u);
         }
         umma_commit_w(&empty[stage]);
         if (++stage == kStages) {
@@ -235,9 +302,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint8_t* buf = sOut + (warp - 2) * Cfg::kOutTile;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+      const GemmUnit un = gemm_unit(u, dp_tiles, splits, num_k);
       int m_blk, n_blk;
-      tile_coords(t, num_m, num_n, m_blk, n_blk);
+      tile_coords(un.tile, num_m, num_n, m_blk, n_blk);
       if (args.m_tiles != nullptr) m_blk = __ldg(args.m_tiles + 1 + m_blk);
       bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
@@ -246,6 +314,57 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int row0 = m_blk * kBM + quad * 32;
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const bool split_tile = un.tile >= dp_tiles;
+      const int tl = un.tile - dp_tiles;  // index among the split tiles
+      // Workspace row of this thread's output row in partial slot p.
+      auto partial_row = [&](int p) {
+        return args.ws + (static_cast<int64_t>(p) * kBM + quad * 32 + lane) * 256;
+      };
+      if (split_tile && un.split > 0) {
+        // ------------------------------------ k-split contributor: fp32 partial
+        float* dst = partial_row(tl * (splits - 1) + un.split - 1);
+#pragma unroll 1
+        for (int c = half; c < BN / 32; c += 2) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c * 32, r);
+          tmem_ld_wait(r);
+          float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            d4[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+        }
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(args.ws_flags + tl, 1);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+        continue;
+      }
+      if (split_tile) {
+        // Owner: the other splits' eight epilogue warps have each counted in.
+        if (lane == 0) wait_count(args.ws_flags + tl, 8 * (splits - 1), abort_flag);
+        __syncwarp();
+      }
+      // Adds the other k-splits' partials for tile columns [c0, c0 + 32).
+      auto add_partials = [&](uint32_t (&r)[32], int c0) {
+        for (int p = 1; p < splits; ++p) {
+          const float4* s4 = reinterpret_cast<const float4*>(partial_row(tl * (splits - 1) + p - 1) + c0);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 q = __ldcg(s4 + i);
+            r[4 * i] = __float_as_uint(__uint_as_float(r[4 * i]) + q.x);
+            r[4 * i + 1] = __float_as_uint(__uint_as_float(r[4 * i + 1]) + q.y);
+            r[4 * i + 2] = __float_as_uint(__uint_as_float(r[4 * i + 2]) + q.z);
+            r[4 * i + 3] = __float_as_uint(__uint_as_float(r[4 * i + 3]) + q.w);
+          }
+        }
+      };
       // One staged 32-row x 128-byte piece: wait until the store that last
       // read this buffer is done, write it, hand it to TMA.
       auto emit = [&](const uint32_t (&w)[32], int col) {
@@ -267,6 +386,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tmem_ld_wait(r);
           const int col0 = n_blk * BN + c * 32;
           if (col0 >= args.N) break;
+          if (split_tile) add_partials(r, c * 32);
           float v[32];
           bias_act(args, col0, r, v);
 #pragma unroll
@@ -279,25 +399,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int col0 = n_blk * BN + c * 64;
           uint32_t w[32];
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
+          for (int hh = 0; hh < 2; ++hh) {
             uint32_t r[32];
-            tmem_ld32(taddr + c * 64 + half * 32, r);
+            tmem_ld32(taddr + c * 64 + hh * 32, r);
             tmem_ld_wait(r);
+            if (split_tile) add_partials(r, c * 64 + hh * 32);
             float v[32];
-            bias_act(args, col0 + half * 32, r, v);
+            bias_act(args, col0 + hh * 32, r, v);
             if (args.out_dtype == TJB_BF16) {
 #pragma unroll
               for (int i = 0; i < 16; ++i)
-                w[half * 16 + i] = Pack2<__nv_bfloat16>::pack(v[2 * i], v[2 * i + 1]);
+                w[hh * 16 + i] = Pack2<__nv_bfloat16>::pack(v[2 * i], v[2 * i + 1]);
             } else {
 #pragma unroll
               for (int i = 0; i < 16; ++i)
-                w[half * 16 + i] = Pack2<__half>::pack(v[2 * i], v[2 * i + 1]);
+                w[hh * 16 + i] = Pack2<__half>::pack(v[2 * i], v[2 * i + 1]);
             }
           }
           if (col0 >= args.N) break;
           emit(w, col0);
         }
+      }
+      if (split_tile) {
+        // This warp has read its share of every partial: give its count back
+        // (eight owner warps return all 8 * (splits - 1) arrivals).
+        __syncwarp();
+        if (lane == 0) atomicSub(args.ws_flags + tl, splits - 1);
       }
       tc_fence_before();
       __syncwarp();
@@ -367,12 +494,16 @@ int launch_gemm(const void* A, const void* B, const GemmArgs& args, int lda, int
 }  // namespace
 }  // namespace tjb
 
-extern "C" int tjb_gemm_bias_tiles(const void* A, const void* B, const float* bias, void* C,
-                                   int M, int N, int K, int lda, int ldb, int ldc, int in_dtype,
-                                   int out_dtype, int act, const int32_t* m_tiles,
-                                   tjb_stream_t stream) {
-  using namespace tjb;
+namespace tjb {
+namespace {
+int gemm_impl(const void* A, const void* B, const float* bias, void* C, int M, int N, int K,
+              int lda, int ldb, int ldc, int in_dtype, int out_dtype, int act,
+              const int32_t* m_tiles, void* workspace, size_t workspace_bytes,
+              tjb_stream_t stream) {
   if (!A || !B || !C || M < 0 || N <= 0 || K <= 0) return TJB_ERR_INVALID_ARGUMENT;
+  if (workspace != nullptr &&
+      (workspace_bytes < tjb_gemm_workspace_bytes() || !aligned16(workspace)))
+    return TJB_ERR_INVALID_ARGUMENT;
   if (in_dtype != TJB_F16 && in_dtype != TJB_BF16) return TJB_ERR_UNSUPPORTED_DTYPE;
   if (out_dtype != TJB_F32 && out_dtype != in_dtype) return TJB_ERR_UNSUPPORTED_DTYPE;
   if (act != 0 && act != 1) return TJB_ERR_INVALID_ARGUMENT;
@@ -393,6 +524,10 @@ extern "C" int tjb_gemm_bias_tiles(const void* A, const void* B, const float* bi
   args.ldc = ldc;
   args.out_dtype = out_dtype;
   args.act = act;
+  args.ws = static_cast<float*>(workspace);
+  args.ws_flags = workspace == nullptr
+                      ? nullptr
+                      : reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + kSkPartialBytes);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int sms = num_sms();
   // Tile width: the fewest waves weighted by each width's time per tile
@@ -415,6 +550,30 @@ extern "C" int tjb_gemm_bias_tiles(const void* A, const void* B, const float* bi
   }
   args.idesc = idesc_f16(kBM, 64, bf16, false);
   return launch_gemm<64>(A, B, args, lda, ldb, bf16, s);
+}
+}  // namespace
+}  // namespace tjb
+
+extern "C" size_t tjb_gemm_workspace_bytes(void) {
+  return tjb::kSkPartialBytes + 256 * sizeof(int);
+}
+
+extern "C" int tjb_gemm_bias_tiles(const void* A, const void* B, const float* bias, void* C,
+                                   int M, int N, int K, int lda, int ldb, int ldc, int in_dtype,
+                                   int out_dtype, int act, const int32_t* m_tiles,
+                                   tjb_stream_t stream) {
+  return tjb::gemm_impl(A, B, bias, C, M, N, K, lda, ldb, ldc, in_dtype, out_dtype, act, m_tiles,
+                        nullptr, 0, stream);
+}
+
+extern "C" int tjb_gemm_bias_tiles_ws(const void* A, const void* B, const float* bias, void* C,
+                                      int M, int N, int K, int lda, int ldb, int ldc,
+                                      int in_dtype, int out_dtype, int act,
+                                      const int32_t* m_tiles, void* workspace,
+                                      size_t workspace_bytes, tjb_stream_t stream) {
+  if (workspace == nullptr) return TJB_ERR_INVALID_ARGUMENT;
+  return tjb::gemm_impl(A, B, bias, C, M, N, K, lda, ldb, ldc, in_dtype, out_dtype, act, m_tiles,
+                        workspace, workspace_bytes, stream);
 }
 
 extern "C" int tjb_gemm_bias(const void* A, const void* B, const float* bias, void* C, int M,

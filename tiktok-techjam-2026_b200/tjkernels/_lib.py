@@ -42,6 +42,12 @@ SIGNATURES = {
                          _c_int, _p]),
     "tjb_ffn_tiles": (_c_int, [_p, _p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int,
                                _c_int, _p, _p]),
+    "tjb_gemm_workspace_bytes": (ctypes.c_size_t, []),
+    "tjb_gemm_bias_tiles_ws": (_c_int, [_p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                        _c_int, _c_int, _c_int, _c_int, _p, _p, ctypes.c_size_t,
+                                        _p]),
+    "tjb_ffn_tiles_ws": (_c_int, [_p, _p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int,
+                                  _c_int, _p, _p, ctypes.c_size_t, _p]),
     "tjb_ffn_fused": (_c_int, [_p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int,
                                _p, _p]),
     "tjb_row_tiles": (_c_int, [_p, _p, _c_int, _c_int, _p, _p]),

@@ -87,6 +87,8 @@ class Engine:
         # Work counter of the dynamic attention schedule: zero between calls
         # (each launch returns it to zero), reused by every layer in order.
         self._attn_sched: Optional[torch.Tensor] = None
+        # Split-K workspace of the GEMMs, shared by all of them in order.
+        self._gemm_ws: Optional[torch.Tensor] = None
 
     # ---------------------------------------------------------------- weights
 
@@ -125,6 +127,7 @@ class Engine:
                              fn.eps)
         self.layers = layers
         self._attn_sched = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self._gemm_ws = K.gemm_workspace(self.device)
         self._built_for = key
         self._graphs.clear()
 
@@ -150,6 +153,7 @@ class Engine:
             res = res.float().contiguous()
         own_res = res.data_ptr() != x.data_ptr()
         delta_dtype = torch.float32 if plan.delta_dtype == torch.float32 else plan.compute_dtype
+        ws = self._gemm_ws if plan.gemm_split_tail else None
         pending: Optional[torch.Tensor] = None
         for lw in self.layers:
             res, h = K.fused_add_layernorm(
@@ -157,20 +161,23 @@ class Engine:
                 residual_out=res if (own_res and pending is not None) else None,
                 m_tiles=tiles)
             own_res = own_res or pending is not None
-            qkv = K.gemm_bias(h, lw.wqkv, lw.bqkv, m_tiles=tiles)
+            qkv = K.gemm_bias(h, lw.wqkv, lw.bqkv, m_tiles=tiles, workspace=ws)
             ctx = K.flash_attention(qkv.view(batch, seq, 3, heads, hd), heads,
                                     causal=self.causal, lengths=lengths, key_mask=mask_u8,
                                     mask_flags=flags, scale=self.scale,
                                     sched=self._attn_sched if plan.attn_dynamic else None)
-            attn_out = K.gemm_bias(ctx, lw.wo, lw.bo, out_dtype=delta_dtype, m_tiles=tiles)
+            attn_out = K.gemm_bias(ctx, lw.wo, lw.bo, out_dtype=delta_dtype, m_tiles=tiles,
+                                   workspace=ws)
             res, h2 = K.fused_add_layernorm(
                 res, attn_out, lw.ln2_w, lw.ln2_b, lw.ln2_eps, out_dtype=plan.compute_dtype,
                 residual_out=res if own_res else None, m_tiles=tiles)
             own_res = True
-            ffn = K.ffn_single_kernel if (plan.ffn_single_kernel and
-                                          K.ffn_fused_supports(d, self.ffn_dim)) else K.fused_ffn
-            pending = ffn(h2, lw.w1, lw.b1, lw.w2, lw.b2, out_dtype=delta_dtype,
-                          m_tiles=tiles)
+            if plan.ffn_single_kernel and K.ffn_fused_supports(d, self.ffn_dim):
+                pending = K.ffn_single_kernel(h2, lw.w1, lw.b1, lw.w2, lw.b2,
+                                              out_dtype=delta_dtype, m_tiles=tiles)
+            else:
+                pending = K.fused_ffn(h2, lw.w1, lw.b1, lw.w2, lw.b2, out_dtype=delta_dtype,
+                                      m_tiles=tiles, workspace=ws)
 
         fw, fb, feps = self.final_ln
         _, out = K.fused_add_layernorm(res, pending, fw, fb, feps, out_dtype=self.dtype,

@@ -1,12 +1,12 @@
 """Run one library kernel on seeded inputs of a given shape (profiling driver).
 
-    python -m tjkernels.kernel_cases gemm M N K [--act gelu] [--out f16|f32] [--launches 3]
+    python -m tjkernels.kernel_cases gemm M N K [--act gelu] [--out f16|f32] [--split-tail] [--launches 3]
     python -m tjkernels.kernel_cases attn B S H HD [--lengths prefix] [--launches 3]
     python -m tjkernels.kernel_cases ln ROWS D [--launches 3]
     python -m tjkernels.kernel_cases ffn T D F [--launches 3]
 
-Each call launches the kernel ``--launches`` times back to back (fp16
-inputs) and prints the CUDA-event time of the last launch.  It is the
+Each call launches the kernel ``--launches`` times (fp16 inputs) and prints
+the median CUDA-event time of all but the first launch.  It is the
 command the ncu summaries of a single kernel are taken with (``ncu -k
 regex:<kernel> -s <n> -c 1 python -m tjkernels.kernel_cases ...``), so a
 capture sees exactly the kernel, shape and launch count named on its line.
@@ -23,15 +23,18 @@ from . import kernels as K
 
 
 def _timed(fn, launches: int) -> float:
-    for _ in range(launches - 1):
-        fn()
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    start.record()
+    """Median CUDA-event time of launches 2..n (the first is a warm-up)."""
     fn()
-    end.record()
-    torch.cuda.synchronize()
-    return start.elapsed_time(end)
+    times = []
+    for _ in range(max(1, launches - 1)):
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        fn()
+        end.record()
+        torch.cuda.synchronize()
+        times.append(start.elapsed_time(end))
+    return sorted(times)[len(times) // 2]
 
 
 def main(argv=None) -> int:
@@ -41,6 +44,8 @@ def main(argv=None) -> int:
     ap.add_argument("--act", choices=["none", "gelu"], default="none")
     ap.add_argument("--out", choices=["f16", "f32"], default="f16")
     ap.add_argument("--lengths", choices=["full", "prefix"], default="full")
+    ap.add_argument("--split-tail", action="store_true",
+                    help="gemm: pass a workspace (split-K tail of the last partial wave)")
     ap.add_argument("--launches", type=int, default=3)
     args = ap.parse_args(argv)
     dev = torch.device("cuda")
@@ -55,7 +60,9 @@ def main(argv=None) -> int:
         bias = torch.randn(n, device=dev, generator=g)
         out_dtype = torch.float16 if args.out == "f16" else torch.float32
         act = K.ACT_GELU if args.act == "gelu" else K.ACT_NONE
-        ms = _timed(lambda: K.gemm_bias(a, w, bias, act=act, out_dtype=out_dtype), args.launches)
+        ws = K.gemm_workspace(dev) if args.split_tail else None
+        ms = _timed(lambda: K.gemm_bias(a, w, bias, act=act, out_dtype=out_dtype, workspace=ws),
+                    args.launches)
         flops = 2.0 * m * n * k
     elif args.kernel == "attn":
         b, s, h, hd = args.dims

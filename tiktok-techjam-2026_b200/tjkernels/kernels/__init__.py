@@ -98,10 +98,12 @@ def layernorm(x, weight, bias, eps, out_dtype=None):
 def gemm_bias(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],
               act: int = ACT_NONE, out_dtype: Optional[torch.dtype] = None,
               out: Optional[torch.Tensor] = None,
-              m_tiles: Optional[torch.Tensor] = None) -> torch.Tensor:
+              m_tiles: Optional[torch.Tensor] = None,
+              workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``act(a @ w.T + bias)``: a ``[M, K]``, w ``[N, K]`` (nn.Linear layout),
     both fp16 or both bf16; bias fp32 ``[N]``; fp32 accumulation.  With
-    ``m_tiles`` only the listed 128-row tiles of the output are computed."""
+    ``m_tiles`` only the listed 128-row tiles of the output are computed.
+    ``workspace`` (see :func:`gemm_workspace`) turns on the split-K tail."""
     _need_cuda(a, w, bias)
     m, k = a.shape
     n, k2 = w.shape
@@ -112,27 +114,50 @@ def gemm_bias(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],
     out_dtype = out_dtype or a.dtype
     if out is None:
         out = torch.empty((m, n), dtype=out_dtype, device=a.device)
-    status = _lib.lib().tjb_gemm_bias_tiles(
-        _ptr(a), _ptr(w), _ptr(bias), _ptr(out), m, n, k, a.stride(0), w.stride(0),
-        out.stride(0), _code(a.dtype), _code(out.dtype), act, _ptr(m_tiles), _stream(a.device))
+    if workspace is not None:
+        status = _lib.lib().tjb_gemm_bias_tiles_ws(
+            _ptr(a), _ptr(w), _ptr(bias), _ptr(out), m, n, k, a.stride(0), w.stride(0),
+            out.stride(0), _code(a.dtype), _code(out.dtype), act, _ptr(m_tiles),
+            _ptr(workspace), workspace.numel() * workspace.element_size(), _stream(a.device))
+    else:
+        status = _lib.lib().tjb_gemm_bias_tiles(
+            _ptr(a), _ptr(w), _ptr(bias), _ptr(out), m, n, k, a.stride(0), w.stride(0),
+            out.stride(0), _code(a.dtype), _code(out.dtype), act, _ptr(m_tiles),
+            _stream(a.device))
     _lib.check(status, "tjb_gemm_bias")
     return out
 
 
+def gemm_workspace(device: torch.device) -> torch.Tensor:
+    """A zeroed split-K workspace for :func:`gemm_bias` / :func:`fused_ffn`
+    (``tjb_gemm_workspace_bytes`` bytes); calls that may overlap on the GPU
+    need separate workspaces."""
+    nbytes = int(_lib.lib().tjb_gemm_workspace_bytes())
+    return torch.zeros(nbytes, dtype=torch.uint8, device=device)
+
+
 def fused_ffn(h: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor, w2: torch.Tensor,
               b2: torch.Tensor, out_dtype: Optional[torch.dtype] = None,
-              m_tiles: Optional[torch.Tensor] = None) -> torch.Tensor:
+              m_tiles: Optional[torch.Tensor] = None,
+              workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``gelu_erf(h @ w1.T + b1) @ w2.T + b2``; w1 ``[F, d]``, w2 ``[d, F]``;
-    with ``m_tiles`` only the listed 128-row tiles are computed."""
+    with ``m_tiles`` only the listed 128-row tiles are computed; ``workspace``
+    turns on the split-K tail of both GEMMs."""
     _need_cuda(h, w1, b1, w2, b2)
     t, d = h.shape
     f = w1.shape[0]
     out_dtype = out_dtype or h.dtype
     out = torch.empty((t, d), dtype=out_dtype, device=h.device)
     hidden = torch.empty((t, f), dtype=h.dtype, device=h.device)
-    status = _lib.lib().tjb_ffn_tiles(
-        _ptr(h), _ptr(w1), _ptr(b1), _ptr(w2), _ptr(b2), _ptr(out), _ptr(hidden), t, d, f,
-        _code(h.dtype), _code(out_dtype), _ptr(m_tiles), _stream(h.device))
+    if workspace is not None:
+        status = _lib.lib().tjb_ffn_tiles_ws(
+            _ptr(h), _ptr(w1), _ptr(b1), _ptr(w2), _ptr(b2), _ptr(out), _ptr(hidden), t, d, f,
+            _code(h.dtype), _code(out_dtype), _ptr(m_tiles), _ptr(workspace),
+            workspace.numel() * workspace.element_size(), _stream(h.device))
+    else:
+        status = _lib.lib().tjb_ffn_tiles(
+            _ptr(h), _ptr(w1), _ptr(b1), _ptr(w2), _ptr(b2), _ptr(out), _ptr(hidden), t, d, f,
+            _code(h.dtype), _code(out_dtype), _ptr(m_tiles), _stream(h.device))
     _lib.check(status, "tjb_ffn")
     return out
 
@@ -236,7 +261,8 @@ def device_status(clear: bool = False) -> int:
 
 
 __all__ = [
-    "ACT_NONE", "ACT_GELU", "fused_add_layernorm", "layernorm", "gemm_bias", "fused_ffn",
+    "ACT_NONE", "ACT_GELU", "fused_add_layernorm", "layernorm", "gemm_bias", "gemm_workspace",
+    "fused_ffn",
     "ffn_single_kernel", "ffn_fused_supports",
     "flash_attention", "flash_supports", "mask_lengths", "row_tiles", "device_status",
 ]

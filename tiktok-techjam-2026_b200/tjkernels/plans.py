@@ -61,6 +61,12 @@ class Plan:
     # rows first) instead of a fixed stride over the CTAs, so that ragged
     # prefix lengths do not leave SMs idle.
     attn_dynamic: bool = True
+    # Split the last partial wave of GEMM tiles along K over the idle SMs
+    # (tjb_gemm_bias_tiles_ws), the partial sums meeting in a workspace.
+    # Off by default: measured slower on B200 (config 2 graph step 1.39 ms
+    # against 0.92; single GEMMs 10-30% slower) -- the owner's reduction of
+    # up to seven fp32 partials through L2 costs more than the idle tail.
+    gemm_split_tail: bool = False
     label: str = "default"
 
     def to_json(self) -> Dict[str, object]:
@@ -72,6 +78,7 @@ class Plan:
             "skip_padding": self.skip_padding,
             "ffn_single_kernel": self.ffn_single_kernel,
             "attn_dynamic": self.attn_dynamic,
+            "gemm_split_tail": self.gemm_split_tail,
             "label": self.label,
         }
 
@@ -154,6 +161,8 @@ def select_plan(batch: int, seq: int, d_model: int, heads: int, ffn_dim: int, la
         plan = replace(plan, skip_padding=False)
     if os.environ.get("TJ_ATTN_STATIC") == "1":
         plan = replace(plan, attn_dynamic=False)
+    if os.environ.get("TJ_SPLIT_TAIL") == "1":
+        plan = replace(plan, gemm_split_tail=True)
     forced = os.environ.get("TJ_DELTA_DTYPE")
     if forced in _DTYPES:
         plan = replace(plan, delta_dtype=_DTYPES[forced])
