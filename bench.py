@@ -17,7 +17,9 @@ CUDA-graph replay included), exactly what the reference harness times.
 L2 is flushed (a 256 MiB write) between timed steps, outside the timed
 events.  ``value`` = all ranks' tokens / max-over-ranks time.
 
-Also reported on the same JSON line:
+Also reported on the same JSON line (scatter_gather only at N > 1: the same
+steps with the inputs on GPU 0, each step scattering the shards over NVLink
+and gathering the outputs back):
   e2e       the same call fed from pinned host memory: host->device copy of x
             and the mask, forward, device->host copy of the output, all timed.
   roofline  the dominant kernel (the tcgen05 GEMM) timed live with CUDA
@@ -445,6 +447,41 @@ def main():
         barrier()
         e2e_ms = e_start.elapsed_time(e_end) / args.steps
 
+        # ------------------------- scatter/gather from GPU 0 (N > 1 only)
+        # The same steps with the inputs starting on GPU 0: each step
+        # scatters the ranks' shards over NVLink (NCCL), runs the forward on
+        # every GPU and gathers the outputs back to GPU 0.
+        sg_ms = 0.0
+        if world > 1:
+            x_all = None
+            out_all = None
+            if rank == 0:
+                x_all = [synthetic_case(b, s, d, 100000, pad, r, world)[0].to(dev)
+                         for r in range(world)]
+                out_all = [torch.empty((b, s, d), dtype=torch.float32, device=dev)
+                           for _ in range(world)]
+            x_sg = torch.empty_like(x)
+
+            def sg_step():
+                dist.scatter(x_sg, x_all, src=0)
+                dist.gather(model(x_sg, mask), out_all, dst=0)
+
+            for _ in range(2):
+                sg_step()
+            torch.cuda.synchronize(dev)
+            barrier()
+            sg_start = torch.cuda.Event(enable_timing=True)
+            sg_end = torch.cuda.Event(enable_timing=True)
+            sg_start.record(stream)
+            for _ in range(args.steps):
+                sg_step()
+                flush.zero_()
+            sg_end.record(stream)
+            torch.cuda.synchronize(dev)
+            barrier()
+            sg_ms = sg_start.elapsed_time(sg_end) / args.steps
+            del x_all, out_all
+
         # -------------------------------------- per-kernel timing (eager)
         ksteps = max(3, min(args.steps, 20))
         plans.set_override(plans.Plan(compute_dtype=plan.compute_dtype,
@@ -460,7 +497,7 @@ def main():
         kern = timer.summary(ksteps)
         plans.set_override(None)
 
-    step_max, e2e_max = max_over_ranks([step_ms, e2e_ms])
+    step_max, e2e_max, sg_max = max_over_ranks([step_ms, e2e_ms, sg_ms])
     launches_per_step = sum(v["launches_per_step"] for v in kern.values())
 
     if rank == 0:
@@ -508,6 +545,12 @@ def main():
             "gpu_launches": int(round(launches_per_step * args.steps)),
             "clocks": clocks.summary(),
         }
+        if world > 1:
+            line["scatter_gather"] = {
+                "value": tokens / (sg_max / 1e3), "unit": "tokens/s", "ms_per_step": sg_max,
+                "bytes_per_step": 2 * (world - 1) * b * s * d * 4,
+                "note": "inputs start on GPU 0; per step NCCL scatter of the shards and "
+                        "gather of the outputs, max over ranks"}
         if world == 1 and not args.no_cpu_baseline:
             sb, sl, calls = cpu_sample_plan(args.config)
             rate, info = cpu_forward_rate(args.config, sb, sl, calls)
