@@ -15,7 +15,7 @@ HEADER = ROOT / "include" / "tjb200.h"
 
 def declared_symbols():
     text = HEADER.read_text()
-    return sorted(set(re.findall(r"^(?:int|const char\*)\s+(tjb_\w+)\(", text, re.M)))
+    return sorted(set(re.findall(r"^(?:int|size_t|const char\*)\s+(tjb_\w+)\(", text, re.M)))
 
 
 def test_library_exports_every_declared_symbol():

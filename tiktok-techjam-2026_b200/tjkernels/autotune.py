@@ -1,0 +1,180 @@
+"""Accuracy-gated plan autotuner: the fastest plan that stays inside the budget.
+
+For one model shape, every candidate :class:`~tjkernels.plans.Plan` is run
+through the engine on seeded inputs, checked against the module's own torch
+forward in fp32 (TF32 off) with the per-element budget
+``|got - ref| <= max(1e-2, 1e-2 |ref|)`` on valid rows (padded rows exactly
+zero), and timed with CUDA events; the fastest passing plan is stored in
+``plans.json`` under the shape key.  Same flow as the reference's
+``bench/autotune.py:58-68,178-246`` (budget-usage gate on held-out seeds,
+then timing), over this engine's knobs.
+
+    python -m tjkernels.autotune B S D H F L [--padding P] [--no-save]
+"""
+
+from __future__ import annotations
+
+import argparse
+import itertools
+import sys
+from dataclasses import replace
+from typing import Dict, Iterable, List, Optional, Tuple
+
+import torch
+
+from . import engine as _engine
+from . import kernels as K
+from . import plans
+
+DEFAULT_LIMIT = 0.5  # fraction of the per-element budget a plan may use
+
+
+def budget_usage(ref: torch.Tensor, got: torch.Tensor) -> float:
+    """max |got - ref| / max(1e-2, 1e-2 |ref|) (1.0 = at the budget)."""
+    tol = torch.clamp(ref.abs() * 1e-2, min=1e-2)
+    return float(((got.double() - ref.double()).abs() / tol.double()).max())
+
+
+def make_inputs(batch: int, seq: int, d_model: int, padding: float, seed: int,
+                device: torch.device) -> Tuple[torch.Tensor, torch.Tensor]:
+    """x ~ N(0,1) with prefix lengths uniform in [max(1, round(S(1-p))), S],
+    padded rows zero (the harness's generate_random_case distribution)."""
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed)
+    x = torch.randn(batch, seq, d_model, generator=g)
+    if padding <= 0:
+        mask = torch.ones(batch, seq, dtype=torch.bool)
+    else:
+        lo = max(1, int(round(seq * (1.0 - padding))))
+        lengths = torch.randint(lo, seq + 1, (batch,), generator=g)
+        mask = torch.arange(seq)[None, :] < lengths[:, None]
+    x = x.masked_fill(~mask[..., None], 0)
+    return x.to(device), mask.to(device)
+
+
+def candidates(d_model: int, ffn_dim: int, base: plans.Plan) -> List[plans.Plan]:
+    """The plan knobs worth sweeping on sm_100a."""
+    out = []
+    single = [False, True] if K.ffn_fused_supports(d_model, ffn_dim) else [False]
+    for cdt, delta32, dyn, split, one in itertools.product(
+            (torch.float16, torch.bfloat16), (False, True), (True, False), (False, True),
+            single):
+        out.append(replace(base, compute_dtype=cdt,
+                           delta_dtype=torch.float32 if delta32 else cdt,
+                           attn_dynamic=dyn, gemm_split_tail=split, ffn_single_kernel=one,
+                           label="tuned"))
+    return out
+
+
+def _reference(module: torch.nn.Module, x: torch.Tensor, mask: torch.Tensor) -> torch.Tensor:
+    """The torch forward in fp32, TF32 off: the harness module's base class
+    (the reference ``BaselineTransformer``), or ``model.torch_forward`` for
+    this package's ``Encoder``."""
+    from .model import Encoder, torch_forward
+
+    prev = (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    try:
+        with torch.no_grad():
+            if isinstance(module, Encoder):
+                return torch_forward(module, x, mask)
+            return super(type(module), module).forward(x, mask)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = prev
+
+
+def _time(fn, reps: int) -> float:
+    fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(reps):
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    return sorted(times)[len(times) // 2]
+
+
+def tune(module: torch.nn.Module, batch: int, seq: int, padding: float = 0.5,
+         seeds: Iterable[int] = (1, 2), limit: float = DEFAULT_LIMIT, reps: int = 10,
+         cands: Optional[List[plans.Plan]] = None, save: bool = True,
+         verbose: bool = False) -> Tuple[plans.Plan, List[Dict[str, object]]]:
+    """Tune ``module`` (a harness-style module whose forward routes to
+    tjkernels and whose base class is the torch reference) for one shape.
+    Returns the chosen plan and one record per candidate."""
+    cfg = module.config
+    device = next(module.parameters()).device
+    if device.type != "cuda":
+        raise RuntimeError("the autotuner runs on CUDA devices only")
+    base = plans.select_plan(batch, seq, cfg.d_model, cfg.num_heads, cfg.ffn_dim,
+                             cfg.num_layers, cfg.causal, next(module.parameters()).dtype, device)
+    cands = cands if cands is not None else candidates(cfg.d_model, cfg.ffn_dim, base)
+    cases = [make_inputs(batch, seq, cfg.d_model, padding, s, device) for s in seeds]
+    refs = [_reference(module, x, m) for x, m in cases]
+    records: List[Dict[str, object]] = []
+    best: Optional[Tuple[float, plans.Plan]] = None
+    try:
+        for plan in cands:
+            plans.set_override(plan)
+            _engine.reset_engines(module)
+            usage, zero_ok = 0.0, True
+            with torch.inference_mode():
+                for (x, m), ref in zip(cases, refs):
+                    got = module(x, m)
+                    usage = max(usage, budget_usage(ref[m], got[m]))
+                    zero_ok = zero_ok and bool((got[~m] == 0).all())
+                ms = _time(lambda: module(cases[0][0], cases[0][1]), reps)
+            ok = zero_ok and usage <= limit
+            records.append({"plan": plan.to_json(), "budget_usage": usage, "ms": ms,
+                            "passes": ok})
+            if verbose:
+                print(f"{plan.to_json()} usage {usage:.3f} {ms:.3f} ms "
+                      f"{'ok' if ok else 'rejected'}", flush=True)
+            if ok and (best is None or ms < best[0]):
+                best = (ms, plan)
+    finally:
+        plans.set_override(None)
+        _engine.reset_engines(module)
+    if best is None:
+        raise RuntimeError("no candidate plan passed the accuracy gate")
+    chosen = best[1]
+    if save:
+        key = plans.shape_key(batch, seq, cfg.d_model, cfg.num_heads, cfg.ffn_dim,
+                              cfg.num_layers, cfg.causal, next(module.parameters()).dtype)
+        table = dict(plans._load_tuned())
+        table[key] = chosen
+        plans.save_plans(table)
+    return chosen, records
+
+
+def main(argv=None) -> int:
+    from .model import Encoder, EncoderConfig
+
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("dims", type=int, nargs=6, metavar=("B", "S", "D", "H", "F", "L"))
+    ap.add_argument("--padding", type=float, default=0.5)
+    ap.add_argument("--limit", type=float, default=DEFAULT_LIMIT)
+    ap.add_argument("--no-save", action="store_true")
+    ap.add_argument("--records", help="write every candidate's record to this JSON file")
+    args = ap.parse_args(argv)
+    b, s, d, h, f, layers = args.dims
+    torch.manual_seed(0)
+    model = Encoder(EncoderConfig(b, s, d, h, f, layers, True)).cuda().eval()
+    plan, records = tune(model, b, s, args.padding, limit=args.limit, save=not args.no_save,
+                         verbose=True)
+    if args.records:
+        import json
+        key = plans.shape_key(b, s, d, h, f, layers, True, torch.float32)
+        with open(args.records, "w") as fh:
+            json.dump({"shape_key": key, "chosen": plan.to_json(), "records": records}, fh,
+                      indent=1)
+    print("chosen:", plan.to_json())
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

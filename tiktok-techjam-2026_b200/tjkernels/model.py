@@ -65,3 +65,54 @@ class Encoder(nn.Module):
     def forward(self, x: torch.Tensor,
                 valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
         return _engine_forward(self, x, valid_token_mask)
+
+
+def torch_forward(module: nn.Module, x: torch.Tensor,
+                  valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The harness's forward in plain torch fp32 on ``module``'s parameters,
+    for accuracy checks (the autotuner's gate), never the engine's path.
+
+    Pre-LN blocks ``x += attn(LN1 x)``, ``x += W2 gelu_erf(W1 LN2 x)``; keys
+    at or above a query (causal) or at padded positions get -inf before an
+    fp32 softmax; padded rows are zeroed after attention, after each block and
+    at the end (``torch_transformer_benchmark.py:66-179``).
+    """
+    import torch.nn.functional as F
+
+    cfg = module.config
+    b, s, d = x.shape
+    heads = cfg.num_heads
+    hd = d // heads
+    mask = valid_token_mask
+    keep = None if mask is None else mask.to(torch.float32)[:, :, None]
+    h = x.float()
+    causal = torch.ones(s, s, dtype=torch.bool, device=x.device).triu(1) if cfg.causal else None
+
+    def lin(layer, t):
+        return F.linear(t, layer.weight.float(), layer.bias.float())
+
+    def ln(norm, t):
+        return F.layer_norm(t, (d,), norm.weight.float(), norm.bias.float(), norm.eps)
+
+    for blk in module.layers:
+        a = ln(blk.norm1, h)
+        att = blk.attention
+        q, k, v = (lin(p, a).view(b, s, heads, hd).transpose(1, 2)
+                   for p in (att.q_proj, att.k_proj, att.v_proj))
+        scores = (q @ k.transpose(-1, -2)) * hd ** -0.5
+        if causal is not None:
+            scores = scores.masked_fill(causal, float("-inf"))
+        if mask is not None:
+            scores = scores.masked_fill(~mask.bool()[:, None, None, :], float("-inf"))
+        ctx = (torch.softmax(scores, dim=-1) @ v).transpose(1, 2).reshape(b, s, d)
+        attn = lin(att.out_proj, ctx)
+        if keep is not None:
+            attn = attn * keep
+        h = h + attn
+        h = h + lin(blk.ffn_out, F.gelu(lin(blk.ffn_in, ln(blk.norm2, h)), approximate="none"))
+        if keep is not None:
+            h = h * keep
+    out = ln(module.final_norm, h)
+    if keep is not None:
+        out = out * keep
+    return out.to(x.dtype)
