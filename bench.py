@@ -320,8 +320,14 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def workload_config(cfg_id, world):
+def workload_config(cfg_id, world, tp=False):
     b, s, d, h, f, layers, pad = CONFIGS[cfg_id]
+    if tp:
+        return {"workload": CONFIG_NOTE[cfg_id] + f" over {world} GPUs", "global_batch": b,
+                "seq_len": s, "d_model": d, "heads": h, "ffn_dim": f, "layers": layers,
+                "parallelism": f"tp{world}: heads and FFN columns split, NCCL all-reduce "
+                               "(fp32) after the out-projection and FFN-out",
+                "l2": "flushed between timed steps (256 MiB write, untimed)"}
     return {"workload": CONFIG_NOTE[cfg_id] + " per GPU", "global_batch": b * world,
             "seq_len": s, "d_model": d, "heads": h, "ffn_dim": f, "layers": layers,
             "parallelism": f"dp{world} batch-sharded, no collective in the forward",
@@ -336,6 +342,9 @@ def main():
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="tjb", choices=["tjb", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp", action="store_true",
+                    help="tensor-parallel over the N GPUs (strong scaling) instead of "
+                         "batch sharding")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -361,7 +370,11 @@ def main():
     cfg = EncoderConfig(b, s, d, h, f, layers, True)
     torch.manual_seed(0)
     model = Encoder(cfg).to(dev).eval()
-    x_cpu, mask_cpu = synthetic_case(b, s, d, 100000, pad, rank, world)
+    tp = args.tp and world > 1
+    if tp:
+        from tjkernels.parallel import enable_tensor_parallel
+        enable_tensor_parallel(model)
+    x_cpu, mask_cpu = synthetic_case(b, s, d, 100000, pad, 0 if tp else rank, 1 if tp else world)
     x, mask = x_cpu.to(dev), mask_cpu.to(dev)
     lengths = mask_cpu.sum(-1).tolist()
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
@@ -452,7 +465,7 @@ def main():
         # scatters the ranks' shards over NVLink (NCCL), runs the forward on
         # every GPU and gathers the outputs back to GPU 0.
         sg_ms = 0.0
-        if world > 1:
+        if world > 1 and not tp:
             x_all = None
             out_all = None
             if rank == 0:
@@ -502,7 +515,7 @@ def main():
 
     if rank == 0:
         peaks = load_peaks()
-        tokens = b * s * world
+        tokens = b * s * (1 if tp else world)
         value = tokens / (step_max / 1e3)
         gemm_ms = (kern["gemm_bias"]["ms_per_step"] + kern["fused_ffn"]["ms_per_step"])
         gemm_flops = (kern["gemm_bias"]["flops_per_call"] * kern["gemm_bias"]["calls_per_step"]
@@ -516,10 +529,11 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_max,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if tp else "weak",
+            "vs_baseline": None,
             "dtype": {torch.float16: "f16", torch.bfloat16: "bf16"}[plan.compute_dtype],
             "data": "synthetic (seeded N(0,1) inputs, default-init weights)",
-            "config": dict(workload_config(args.config, world),
+            "config": dict(workload_config(args.config, world, tp),
                            plan=plan.to_json()),
             "roofline": {
                 "bound": "tensor", "kernel": "gemm_kernel (tcgen05, all GEMM launches)",
@@ -545,7 +559,7 @@ def main():
             "gpu_launches": int(round(launches_per_step * args.steps)),
             "clocks": clocks.summary(),
         }
-        if world > 1:
+        if world > 1 and not tp:
             line["scatter_gather"] = {
                 "value": tokens / (sg_max / 1e3), "unit": "tokens/s", "ms_per_step": sg_max,
                 "bytes_per_step": 2 * (world - 1) * b * s * d * 4,

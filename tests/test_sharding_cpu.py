@@ -126,3 +126,65 @@ def test_balanced_equal_shards():
         assert max(work) / min(work) < 1.15
     with pytest.raises(ValueError):
         balanced_equal_shards([1, 2, 3], 2)
+
+
+def _tp_worker(rank, world, port, out_q):
+    import os
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle.model import ModelConfig, generate_case
+        from tjkernels.model import Encoder, EncoderConfig
+        from tjkernels.parallel import tp_torch_forward
+        cfg = ModelConfig(2, 40, 128, 4, 256, 2, True)
+        torch.manual_seed(0)
+        enc = Encoder(EncoderConfig(2, 40, 128, 4, 256, 2, True))
+        x, mask = generate_case(cfg, 5, 0.5)
+        with torch.no_grad():
+            out = tp_torch_forward(enc, x, mask, rank, world)
+        out_q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tensor_parallel_math_matches_unsharded(world):
+    """Column-parallel QKV / FFN-in, row-parallel out-proj / FFN-out with an
+    all-reduce (gloo ranks on the CPU) give every rank the unsharded forward."""
+    import torch.multiprocessing as mp
+    from oracle.model import ModelConfig, generate_case
+    from tjkernels.model import Encoder, EncoderConfig, torch_forward
+    cfg = ModelConfig(2, 40, 128, 4, 256, 2, True)
+    torch.manual_seed(0)
+    enc = Encoder(EncoderConfig(2, 40, 128, 4, 256, 2, True))
+    x, mask = generate_case(cfg, 5, 0.5)
+    with torch.no_grad():
+        want = torch_forward(enc, x, mask)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29600 + world
+    procs = [ctx.Process(target=_tp_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    outs = dict(q.get(timeout=180) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(world):
+        assert (outs[r] - want).abs().max().item() < 1e-4
+        assert bool((outs[r][~mask] == 0).all())
+
+
+def test_tp_shard_shapes_and_errors():
+    from tjkernels.model import Encoder, EncoderConfig
+    from tjkernels.parallel import tp_shard
+    torch.manual_seed(0)
+    enc = Encoder(EncoderConfig(1, 8, 64, 4, 256, 1, True))
+    w = tp_shard(enc.layers[0], 1, 4)
+    assert w["wqkv"].shape == (48, 64) and w["wo"].shape == (64, 16)
+    assert w["w1"].shape == (64, 64) and w["w2"].shape == (64, 64)
+    assert torch.equal(w["wqkv"][:16], enc.layers[0].attention.q_proj.weight[16:32])
+    with pytest.raises(ValueError):
+        tp_shard(enc.layers[0], 0, 3)

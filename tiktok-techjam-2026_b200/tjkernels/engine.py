@@ -84,6 +84,10 @@ class Engine:
         self.final_ln: Optional[Tuple[torch.Tensor, torch.Tensor, float]] = None
         self._module = module
         self._graphs = GraphCache()
+        # Tensor-parallel layout (parallel.enable_tensor_parallel): this rank
+        # keeps num_heads/W heads and ffn_dim/W FFN columns; the partial
+        # outputs of the out-projection and FFN-out are all-reduced.
+        self._tp = getattr(module, "_tj_tp", None)
         # Work counter of the dynamic attention schedule: zero between calls
         # (each launch returns it to zero), reused by every layer in order.
         self._attn_sched: Optional[torch.Tensor] = None
@@ -99,6 +103,9 @@ class Engine:
             return
         cdt = plan.compute_dtype
         layers: List[LayerWeights] = []
+        if self._tp is not None:
+            self._build_tp(plan)
+            return
         with torch.no_grad():
             for block in self._module.layers:
                 attn = block.attention
@@ -131,6 +138,43 @@ class Engine:
         self._built_for = key
         self._graphs.clear()
 
+    def _build_tp(self, plan: Plan) -> None:
+        """This rank's slice of every block (tensor-parallel layout); the
+        row-parallel biases stay on rank 0 only (zero elsewhere)."""
+        from .parallel import tp_shard
+
+        _, rank, world = self._tp
+        cdt = plan.compute_dtype
+        layers: List[LayerWeights] = []
+        with torch.no_grad():
+            for block in self._module.layers:
+                w = tp_shard(block, rank, world)
+                keep = 1.0 if rank == 0 else 0.0
+                layers.append(LayerWeights(
+                    ln1_w=block.norm1.weight.float().contiguous(),
+                    ln1_b=block.norm1.bias.float().contiguous(),
+                    ln1_eps=block.norm1.eps,
+                    wqkv=w["wqkv"].to(cdt).contiguous(),
+                    bqkv=w["bqkv"].float().contiguous(),
+                    wo=w["wo"].to(cdt).contiguous(),
+                    bo=(w["bo"].float() * keep).contiguous(),
+                    ln2_w=block.norm2.weight.float().contiguous(),
+                    ln2_b=block.norm2.bias.float().contiguous(),
+                    ln2_eps=block.norm2.eps,
+                    w1=w["w1"].to(cdt).contiguous(),
+                    b1=w["b1"].float().contiguous(),
+                    w2=w["w2"].to(cdt).contiguous(),
+                    b2=(w["b2"].float() * keep).contiguous(),
+                ))
+            fn = self._module.final_norm
+            self.final_ln = (fn.weight.float().contiguous(), fn.bias.float().contiguous(),
+                             fn.eps)
+        self.layers = layers
+        self._attn_sched = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self._gemm_ws = K.gemm_workspace(self.device)
+        self._built_for = (plan.compute_dtype, self.dtype, self.device)
+        self._graphs.clear()
+
     # ---------------------------------------------------------------- compute
 
     def _forward_impl(self, x: torch.Tensor, mask: Optional[torch.Tensor]) -> torch.Tensor:
@@ -139,6 +183,12 @@ class Engine:
         batch, seq, d = x.shape
         tokens = batch * seq
         heads, hd = self.num_heads, self.head_dim
+        tp_on = self._tp is not None  # (the group itself may be None: the world)
+        tp_group = None
+        if tp_on:
+            import torch.distributed as dist
+            tp_group, _, tp_world = self._tp
+            heads //= tp_world
 
         mask_u8 = lengths = flags = tiles = None
         if mask is not None:
@@ -153,6 +203,8 @@ class Engine:
             res = res.float().contiguous()
         own_res = res.data_ptr() != x.data_ptr()
         delta_dtype = torch.float32 if plan.delta_dtype == torch.float32 else plan.compute_dtype
+        if tp_on:
+            delta_dtype = torch.float32  # partial sums are all-reduced in fp32
         ws = self._gemm_ws if plan.gemm_split_tail else None
         pending: Optional[torch.Tensor] = None
         for lw in self.layers:
@@ -168,16 +220,21 @@ class Engine:
                                     sched=self._attn_sched if plan.attn_dynamic else None)
             attn_out = K.gemm_bias(ctx, lw.wo, lw.bo, out_dtype=delta_dtype, m_tiles=tiles,
                                    workspace=ws)
+            if tp_on:
+                dist.all_reduce(attn_out, group=tp_group)
             res, h2 = K.fused_add_layernorm(
                 res, attn_out, lw.ln2_w, lw.ln2_b, lw.ln2_eps, out_dtype=plan.compute_dtype,
                 residual_out=res if own_res else None, m_tiles=tiles)
             own_res = True
-            if plan.ffn_single_kernel and K.ffn_fused_supports(d, self.ffn_dim):
+            if (plan.ffn_single_kernel and not tp_on and
+                    K.ffn_fused_supports(d, self.ffn_dim)):
                 pending = K.ffn_single_kernel(h2, lw.w1, lw.b1, lw.w2, lw.b2,
                                               out_dtype=delta_dtype, m_tiles=tiles)
             else:
                 pending = K.fused_ffn(h2, lw.w1, lw.b1, lw.w2, lw.b2, out_dtype=delta_dtype,
                                       m_tiles=tiles, workspace=ws)
+            if tp_on:
+                dist.all_reduce(pending, group=tp_group)
 
         fw, fb, feps = self.final_ln
         _, out = K.fused_add_layernorm(res, pending, fw, fb, feps, out_dtype=self.dtype,
@@ -198,7 +255,7 @@ class Engine:
                 self._plan_cache[(batch, seq)] = plan
         self.plan = plan
         self._build(plan)
-        if plan.cuda_graph:
+        if plan.cuda_graph and self._tp is None:
             key = (tuple(x.shape), x.dtype, mask is not None, plan)
             return self._graphs.get(key, self._forward_impl, x, mask).run(x, mask)
         return self._forward_impl(x, mask)
