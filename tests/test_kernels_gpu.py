@@ -196,6 +196,23 @@ def test_flash_dense(b, s, h, hd, causal, dtype):
 
 @pytest.mark.parametrize("causal", [True, False])
 @pytest.mark.parametrize("hd", [64, 128])
+def test_flash_growing_scores_rescale(causal, hd):
+    """Key norms growing along the sequence push a row's running max up by far
+    more than the lazy-rescale threshold several times after the first key
+    tile, so the output accumulator is rescaled in tensor memory mid-row."""
+    b, s, h = 2, 1000, 2
+    g = torch.Generator(device=DEV).manual_seed(31 + hd)
+    qkv = torch.randn(b, s, 3, h, hd, device=DEV, generator=g)
+    qkv[:, :, 1] *= (1.0 + torch.arange(s, device=DEV) / 64.0).clamp(max=8.0)[None, :, None, None]
+    qkv = qkv.half()
+    out = K().flash_attention(qkv, h, causal=causal)
+    ref = attn_reference(qkv, causal)
+    err = (out.double() - ref).abs().max().item()
+    assert err < 4e-3, err
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("hd", [64, 128])
 def test_flash_prefix_lengths(causal, hd):
     b, s, h = 4, 700, 2
     qkv = torch.randn(b, s, 3, h, hd, device=DEV).bfloat16()
