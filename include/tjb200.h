@@ -121,10 +121,12 @@ int tjb_gemm_bias_tiles(const void* A, const void* B, const float* bias, void* C
 size_t tjb_gemm_workspace_bytes(void);
 
 /*
- * tjb_gemm_bias_tiles with a split-K tail: when the output tiles do not fill
- * a whole number of waves over the SMs, each tile of the last partial wave
- * is split along K over CTAs that would otherwise idle, the partial sums
- * meeting in the workspace (fp32).  workspace: tjb_gemm_workspace_bytes()
+ * tjb_gemm_bias_tiles with stream-K: when K spans at least 48 k-blocks of 64
+ * and the last wave of output tiles would leave at least three quarters of
+ * the SMs idle, the tiles' k-blocks are divided into one equal run per CTA;
+ * a tile whose k-blocks fall into two or three runs has its partial sums
+ * (fp32) meet in the workspace, added by the CTA holding its first k-block.
+ * Other shapes run as tjb_gemm_bias_tiles.  workspace: tjb_gemm_workspace_bytes()
  * bytes of device memory, 16-byte aligned, zero-filled before its first use;
  * each call leaves it ready for the next.  Calls that may run at the same
  * time need separate workspaces.  Same result layout as
@@ -190,7 +192,7 @@ int tjb_ffn_tiles(const void* h, const void* w1, const float* b1, const void* w2
                   const float* b2, void* out, void* hidden, int T, int d, int F,
                   int in_dtype, int out_dtype, const int32_t* m_tiles, tjb_stream_t stream);
 
-/* tjb_ffn_tiles whose two GEMMs use the split-K tail (see
+/* tjb_ffn_tiles whose two GEMMs may use stream-K (see
  * tjb_gemm_bias_tiles_ws; one workspace serves both, they run in order). */
 int tjb_ffn_tiles_ws(const void* h, const void* w1, const float* b1, const void* w2,
                      const float* b2, void* out, void* hidden, int T, int d, int F,

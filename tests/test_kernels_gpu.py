@@ -89,17 +89,21 @@ def test_gemm_bias(m, n, k, dtype):
     assert ((out16.double() - ref).abs() <= tol * ref.abs() + 1e-3 * scale).all()
 
 
-SPLIT_SHAPES = [(5120, 1024, 1024), (5120, 1024, 4096), (4608, 3072, 1024), (300, 136, 512),
-                (2000, 1032, 2048), (129, 64, 64)]
+# Stream-K runs for (5120, 1024, 4096), (5376, 1024, 3072), (9600, 1024, 4096)
+# and (4480, 1032, 4096) (a partial last column tile); the other shapes take
+# the whole-tile path with a workspace passed.
+SPLIT_SHAPES = [(5120, 1024, 1024), (5120, 1024, 4096), (5376, 1024, 3072), (9600, 1024, 4096),
+                (4480, 1032, 4096), (4608, 3072, 1024), (300, 136, 512), (2000, 1032, 2048),
+                (129, 64, 64)]
 
 
 @pytest.mark.parametrize("m,n,k", SPLIT_SHAPES)
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16])
-def test_gemm_split_tail(m, n, k, out_dtype):
-    """The split-K tail (last partial wave of tiles split along K over idle
-    SMs, partials meeting in the workspace) matches fp64 and the whole-tile
-    kernel, with GELU and a live-tile list too, and leaves the workspace's
-    counters at zero for the next call."""
+def test_gemm_stream_k(m, n, k, out_dtype):
+    """Stream-K (equal k-block runs per CTA, split tiles' partials meeting in
+    the workspace) matches fp64 and the whole-tile kernel, with GELU and a
+    live-tile list too, and leaves the workspace's counters at zero for the
+    next call."""
     g = torch.Generator(device=DEV).manual_seed(m * 7 + n + k)
     a = torch.randn(m, k, device=DEV, generator=g).half()
     w = (torch.randn(n, k, device=DEV, generator=g) / math.sqrt(k)).half()

@@ -58,36 +58,50 @@ struct GemmArgs {
   int* ws_flags;  // [kSkMaxPartials] arrival counts, zero between launches
 };
 
-// Split-K tail.  When the tiles do not fill a whole number of waves over the
-// grid, the leftover tiles of the last wave are each split along K over
-// `splits` CTAs that would otherwise idle: the CTA holding k-split 0 owns the
-// tile, the others write fp32 partials into the workspace and count in
-// ws_flags; the owner adds them before its epilogue and returns the count to
-// zero.  A work unit is a whole tile (the first dp_tiles) or one k-split.
-constexpr int kSkMaxSplits = 8;
-constexpr int kSkMaxPartials = 160;  // >= grid - leftover tiles
+// Stream-K.  When the output tiles do not fill a whole number of waves over
+// the grid (at least a quarter of the CTAs would idle in the last wave), the
+// k-blocks of all tiles are laid end to end (tile-major) and every CTA takes
+// one contiguous run of ceil(tiles * k_blocks / grid) of them.  A run covers
+// whole tiles plus at most a tail piece of one tile at its start and a head
+// piece of another at its end.  The CTA holding a tile's first k-block owns
+// the tile; the CTAs holding the rest of it (its piece is the first of their
+// runs, so they finish it early) write fp32 partials into their own
+// workspace slot and count in; the owner (whose head piece is the last of its
+// run) adds them before its epilogue and returns the counts to zero.
+// Measured on a B200 (fp16, 128x256 tiles): a split tile costs its owner
+// ~3 us (waiting for and adding the partial), so the rebalancing pays only
+// for long tiles (K = 4096 with one tile in twelve left over: 48 -> 41 us)
+// and loses for K = 1024 or a last wave more than a quarter full.
+constexpr int kSkMinKBlocks = 48;
+constexpr int kSkMaxPartials = 160;  // workspace slots: one per CTA, >= grid
 constexpr size_t kSkPartialBytes = static_cast<size_t>(kSkMaxPartials) * kBM * 256 * 4;
 
-struct GemmUnit {
-  int tile, split, kb0, kb1;
+struct GemmPiece {
+  int tile, kb0, kb1;  // k-blocks [kb0, kb1) of output tile `tile`
 };
 
-__device__ __forceinline__ GemmUnit gemm_unit(int u, int dp_tiles, int splits, int num_k) {
-  GemmUnit x;
-  if (u < dp_tiles) {
-    x.tile = u;
-    x.split = 0;
-    x.kb0 = 0;
-    x.kb1 = num_k;
-    return x;
+// This CTA's work in order: whole tiles at a stride of the grid, or the
+// pieces of its stream-K run [cursor, end) of the tile-major k-block space.
+struct PieceIter {
+  int cursor, end, num_k, num_tiles, stride;
+  bool sk;
+  __device__ __forceinline__ bool next(GemmPiece& p) {
+    if (!sk) {
+      if (cursor >= num_tiles) return false;
+      p.tile = cursor;
+      p.kb0 = 0;
+      p.kb1 = num_k;
+      cursor += stride;
+      return true;
+    }
+    if (cursor >= end) return false;
+    p.tile = cursor / num_k;
+    p.kb0 = cursor - p.tile * num_k;
+    p.kb1 = min(num_k, end - p.tile * num_k);
+    cursor = p.tile * num_k + p.kb1;
+    return true;
   }
-  const int l = u - dp_tiles;
-  x.tile = dp_tiles + l / splits;
-  x.split = l % splits;
-  x.kb0 = x.split * num_k / splits;
-  x.kb1 = (x.split + 1) * num_k / splits;
-  return x;
-}
+};
 
 // Bounded wait until *count reaches target (acquire).
 __device__ __forceinline__ bool wait_count(const int* count, int target, volatile int* abort) {
@@ -206,19 +220,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int num_n = (args.N + BN - 1) / BN;
   const int num_k = (args.K + kBK - 1) / kBK;
   const int num_tiles = num_m * num_n;
-  int dp_tiles = num_tiles, splits = 1;
-  if (args.ws != nullptr) {
-    const int grid = static_cast<int>(gridDim.x);
+  const int grid = static_cast<int>(gridDim.x);
+  bool sk = false;
+  int sk_w = 0;  // k-blocks per CTA run
+  if (args.ws != nullptr && grid <= kSkMaxPartials && num_k >= kSkMinKBlocks) {
     const int rem = num_tiles % grid;
-    if (rem > 0) {
-      const int sk = min(min(grid / rem, kSkMaxSplits), num_k / 2);
-      if (sk >= 2) {
-        dp_tiles = num_tiles - rem;
-        splits = sk;
-      }
+    // A last wave at most a quarter full, and at least half a tile per CTA
+    // (so a tile is split over at most three runs).
+    if (rem != 0 && 4 * (grid - rem) >= 3 * grid && 2 * num_tiles >= grid) {
+      sk = true;
+      sk_w = (num_tiles * num_k + grid - 1) / grid;
     }
   }
-  const int num_units = dp_tiles + (num_tiles - dp_tiles) * splits;
+  auto pieces = [&]() {
+    PieceIter it;
+    it.num_k = num_k;
+    it.num_tiles = num_tiles;
+    it.stride = grid;
+    it.sk = sk;
+    it.cursor = sk ? static_cast<int>(blockIdx.x) * sk_w : static_cast<int>(blockIdx.x);
+    it.end = sk ? min((static_cast<int>(blockIdx.x) + 1) * sk_w, num_tiles * num_k) : 0;
+    return it;
+  };
 
   if (warp == 0) {
     if (lane == 0) {
@@ -226,8 +249,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0, issued = 0, issued_parity = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-        const GemmUnit un = gemm_unit(u, dp_tiles, splits, num_k);
+      PieceIter it = pieces();
+      GemmPiece un;
+      while (ok && it.next(un)) {
         int m_blk, n_blk;
         tile_coords(un.tile, num_m, num_n, m_blk, n_blk);
         if (args.m_tiles != nullptr) m_blk = __ldg(args.m_tiles + 1 + m_blk);
@@ -260,8 +284,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     auto wait = [&](uint64_t* bar, uint32_t parity) {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
     };
-    for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-      const GemmUnit un = gemm_unit(u, dp_tiles, splits, num_k);
+    PieceIter it = pieces();
+    GemmPiece un;
+    while (ok && it.next(un)) {
       if (!wait(&tempty[acc], acc_phase ^ 1)) break;
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -302,8 +327,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint8_t* buf = sOut + (warp - 2) * Cfg::kOutTile;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
-      const GemmUnit un = gemm_unit(u, dp_tiles, splits, num_k);
+    PieceIter it = pieces();
+    GemmPiece un;
+    while (it.next(un)) {
       int m_blk, n_blk;
       tile_coords(un.tile, num_m, num_n, m_blk, n_blk);
       if (args.m_tiles != nullptr) m_blk = __ldg(args.m_tiles + 1 + m_blk);
@@ -314,29 +340,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int row0 = m_blk * kBM + quad * 32;
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      const bool split_tile = un.tile >= dp_tiles;
-      const int tl = un.tile - dp_tiles;  // index among the split tiles
-      // Workspace row of this thread's output row in partial slot p.
-      auto partial_row = [&](int p) {
-        return args.ws + (static_cast<int64_t>(p) * kBM + quad * 32 + lane) * 256;
+      // Stream-K roles: a piece that starts past k-block 0 is a contributor
+      // (it writes this CTA's partial slot); a piece that starts at 0 but
+      // stops short of the end is the owner, and CTAs blockIdx.x + 1 ..
+      // c_last hold the rest of its tile.
+      const bool contributor = un.kb0 > 0;
+      const bool owner = un.kb0 == 0 && un.kb1 < num_k;
+      const int c_last = owner ? ((un.tile + 1) * num_k - 1) / sk_w : 0;
+      // Partial slots are column-major ([slot][column][row], fp32), so one
+      // warp-wide access of column j touches 32 consecutive rows = one
+      // 128-byte line.  This thread's element of column j in slot p:
+      auto partial_at = [&](int p, int j) {
+        return args.ws + (static_cast<int64_t>(p) * 256 + j) * kBM + quad * 32 + lane;
       };
-      if (split_tile && un.split > 0) {
-        // ------------------------------------ k-split contributor: fp32 partial
-        float* dst = partial_row(tl * (splits - 1) + un.split - 1);
+      if (contributor) {
+        // ------------------------------------ stream-K contributor: fp32 partial
 #pragma unroll 1
         for (int c = half; c < BN / 32; c += 2) {
           uint32_t r[32];
           tmem_ld32(taddr + c * 32, r);
           tmem_ld_wait(r);
-          float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            d4[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
-                                __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+          for (int i = 0; i < 32; ++i) __stcg(partial_at(blockIdx.x, c * 32 + i), __uint_as_float(r[i]));
         }
         __threadfence();
         __syncwarp();
-        if (lane == 0) atomicAdd(args.ws_flags + tl, 1);
+        if (lane == 0) atomicAdd(args.ws_flags + blockIdx.x, 1);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -346,23 +375,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         continue;
       }
-      if (split_tile) {
-        // Owner: the other splits' eight epilogue warps have each counted in.
-        if (lane == 0) wait_count(args.ws_flags + tl, 8 * (splits - 1), abort_flag);
+      if (owner) {
+        // Each contributor's eight epilogue warps have counted in.
+        if (lane == 0)
+          for (int c = blockIdx.x + 1; c <= c_last; ++c) wait_count(args.ws_flags + c, 8, abort_flag);
         __syncwarp();
       }
-      // Adds the other k-splits' partials for tile columns [c0, c0 + 32).
+      // Adds the contributors' partials for tile columns [c0, c0 + 32).
       auto add_partials = [&](uint32_t (&r)[32], int c0) {
-        for (int p = 1; p < splits; ++p) {
-          const float4* s4 = reinterpret_cast<const float4*>(partial_row(tl * (splits - 1) + p - 1) + c0);
+        for (int p = blockIdx.x + 1; p <= c_last; ++p) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float4 q = __ldcg(s4 + i);
-            r[4 * i] = __float_as_uint(__uint_as_float(r[4 * i]) + q.x);
-            r[4 * i + 1] = __float_as_uint(__uint_as_float(r[4 * i + 1]) + q.y);
-            r[4 * i + 2] = __float_as_uint(__uint_as_float(r[4 * i + 2]) + q.z);
-            r[4 * i + 3] = __float_as_uint(__uint_as_float(r[4 * i + 3]) + q.w);
-          }
+          for (int i = 0; i < 32; ++i)
+            r[i] = __float_as_uint(__uint_as_float(r[i]) + __ldcg(partial_at(p, c0 + i)));
         }
       };
       // One staged 32-row x 128-byte piece: wait until the store that last
@@ -386,7 +410,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tmem_ld_wait(r);
           const int col0 = n_blk * BN + c * 32;
           if (col0 >= args.N) break;
-          if (split_tile) add_partials(r, c * 32);
+          if (owner) add_partials(r, c * 32);
           float v[32];
           bias_act(args, col0, r, v);
 #pragma unroll
@@ -403,7 +427,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             uint32_t r[32];
             tmem_ld32(taddr + c * 64 + hh * 32, r);
             tmem_ld_wait(r);
-            if (split_tile) add_partials(r, c * 64 + hh * 32);
+            if (owner) add_partials(r, c * 64 + hh * 32);
             float v[32];
             bias_act(args, col0 + hh * 32, r, v);
             if (args.out_dtype == TJB_BF16) {
@@ -420,11 +444,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           emit(w, col0);
         }
       }
-      if (split_tile) {
-        // This warp has read its share of every partial: give its count back
-        // (eight owner warps return all 8 * (splits - 1) arrivals).
+      if (owner) {
+        // This warp has read its share of every partial: give one count back
+        // per contributor (the owner's eight warps return all eight).
         __syncwarp();
-        if (lane == 0) atomicSub(args.ws_flags + tl, splits - 1);
+        if (lane == 0)
+          for (int c = blockIdx.x + 1; c <= c_last; ++c) atomicSub(args.ws_flags + c, 1);
       }
       tc_fence_before();
       __syncwarp();
@@ -535,8 +560,14 @@ int gemm_impl(const void* A, const void* B, const float* bias, void* C, int M, i
   // N 1024-4096, K 1024-4096: 0.65 for 128-wide, 0.5 for 64-wide).  With a
   // live-tile list the listed count is not known on the host, so M is taken
   // as given.
+  // With a stream-K workspace a partial last wave costs only its share of the
+  // k-blocks, so the widest (most efficient) tile wins whenever N allows it.
   const long mt = (M + kBM - 1) / kBM;
   auto waves = [&](int bn) { return (mt * ((N + bn - 1) / bn) + sms - 1) / sms; };
+  if (workspace != nullptr && N >= 256 && (K + kBK - 1) / kBK >= kSkMinKBlocks) {
+    args.idesc = idesc_f16(kBM, 256, bf16, false);
+    return launch_gemm<256>(A, B, args, lda, ldb, bf16, s);
+  }
   const double c256 = N >= 256 ? static_cast<double>(waves(256)) : 1e30;
   const double c128 = N >= 128 ? waves(128) * 0.65 : 1e30;
   const double c64 = waves(64) * 0.5;

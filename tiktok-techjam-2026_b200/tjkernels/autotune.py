@@ -61,7 +61,7 @@ def candidates(d_model: int, ffn_dim: int, base: plans.Plan) -> List[plans.Plan]
             single):
         out.append(replace(base, compute_dtype=cdt,
                            delta_dtype=torch.float32 if delta32 else cdt,
-                           attn_dynamic=dyn, gemm_split_tail=split, ffn_single_kernel=one,
+                           attn_dynamic=dyn, gemm_stream_k=split, ffn_single_kernel=one,
                            label="tuned"))
     return out
 

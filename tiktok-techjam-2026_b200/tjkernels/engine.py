@@ -205,7 +205,7 @@ class Engine:
         delta_dtype = torch.float32 if plan.delta_dtype == torch.float32 else plan.compute_dtype
         if tp_on:
             delta_dtype = torch.float32  # partial sums are all-reduced in fp32
-        ws = self._gemm_ws if plan.gemm_split_tail else None
+        ws = self._gemm_ws if plan.gemm_stream_k else None
         pending: Optional[torch.Tensor] = None
         for lw in self.layers:
             res, h = K.fused_add_layernorm(

@@ -1,6 +1,6 @@
 """Run one library kernel on seeded inputs of a given shape (profiling driver).
 
-    python -m tjkernels.kernel_cases gemm M N K [--act gelu] [--out f16|f32] [--split-tail] [--launches 3]
+    python -m tjkernels.kernel_cases gemm M N K [--act gelu] [--out f16|f32] [--stream-k] [--launches 3]
     python -m tjkernels.kernel_cases attn B S H HD [--lengths prefix] [--launches 3]
     python -m tjkernels.kernel_cases ln ROWS D [--launches 3]
     python -m tjkernels.kernel_cases ffn T D F [--launches 3]
@@ -44,8 +44,8 @@ def main(argv=None) -> int:
     ap.add_argument("--act", choices=["none", "gelu"], default="none")
     ap.add_argument("--out", choices=["f16", "f32"], default="f16")
     ap.add_argument("--lengths", choices=["full", "prefix"], default="full")
-    ap.add_argument("--split-tail", action="store_true",
-                    help="gemm: pass a workspace (split-K tail of the last partial wave)")
+    ap.add_argument("--stream-k", action="store_true",
+                    help="gemm: pass a stream-K workspace")
     ap.add_argument("--launches", type=int, default=3)
     args = ap.parse_args(argv)
     dev = torch.device("cuda")
@@ -60,7 +60,7 @@ def main(argv=None) -> int:
         bias = torch.randn(n, device=dev, generator=g)
         out_dtype = torch.float16 if args.out == "f16" else torch.float32
         act = K.ACT_GELU if args.act == "gelu" else K.ACT_NONE
-        ws = K.gemm_workspace(dev) if args.split_tail else None
+        ws = K.gemm_workspace(dev) if args.stream_k else None
         ms = _timed(lambda: K.gemm_bias(a, w, bias, act=act, out_dtype=out_dtype, workspace=ws),
                     args.launches)
         flops = 2.0 * m * n * k

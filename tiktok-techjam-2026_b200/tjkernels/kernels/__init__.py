@@ -103,7 +103,7 @@ def gemm_bias(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],
     """``act(a @ w.T + bias)``: a ``[M, K]``, w ``[N, K]`` (nn.Linear layout),
     both fp16 or both bf16; bias fp32 ``[N]``; fp32 accumulation.  With
     ``m_tiles`` only the listed 128-row tiles of the output are computed.
-    ``workspace`` (see :func:`gemm_workspace`) turns on the split-K tail."""
+    ``workspace`` (see :func:`gemm_workspace`) lets the kernel use stream-K."""
     _need_cuda(a, w, bias)
     m, k = a.shape
     n, k2 = w.shape
@@ -142,7 +142,7 @@ def fused_ffn(h: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor, w2: torch.Ten
               workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``gelu_erf(h @ w1.T + b1) @ w2.T + b2``; w1 ``[F, d]``, w2 ``[d, F]``;
     with ``m_tiles`` only the listed 128-row tiles are computed; ``workspace``
-    turns on the split-K tail of both GEMMs."""
+    lets both GEMMs use stream-K."""
     _need_cuda(h, w1, b1, w2, b2)
     t, d = h.shape
     f = w1.shape[0]

@@ -61,12 +61,12 @@ class Plan:
     # rows first) instead of a fixed stride over the CTAs, so that ragged
     # prefix lengths do not leave SMs idle.
     attn_dynamic: bool = True
-    # Split the last partial wave of GEMM tiles along K over the idle SMs
-    # (tjb_gemm_bias_tiles_ws), the partial sums meeting in a workspace.
-    # Off by default: measured slower on B200 (config 2 graph step 1.39 ms
-    # against 0.92; single GEMMs 10-30% slower) -- the owner's reduction of
-    # up to seven fp32 partials through L2 costs more than the idle tail.
-    gemm_split_tail: bool = False
+    # Give the GEMMs a workspace for stream-K (tjb_gemm_bias_tiles_ws): when a
+    # long-K GEMM's last wave of tiles would leave at least three quarters of
+    # the SMs idle, every CTA takes an equal run of k-blocks and split tiles
+    # meet in the workspace.  The kernel decides per launch from the live
+    # tile count; shapes outside that window run unchanged.
+    gemm_stream_k: bool = True
     label: str = "default"
 
     def to_json(self) -> Dict[str, object]:
@@ -78,7 +78,7 @@ class Plan:
             "skip_padding": self.skip_padding,
             "ffn_single_kernel": self.ffn_single_kernel,
             "attn_dynamic": self.attn_dynamic,
-            "gemm_split_tail": self.gemm_split_tail,
+            "gemm_stream_k": self.gemm_stream_k,
             "label": self.label,
         }
 
@@ -88,6 +88,9 @@ class Plan:
         for key, default in (("compute_dtype", "float16"), ("residual_dtype", "float32"),
                              ("delta_dtype", "float16")):
             blob[key] = _DTYPES[str(blob.get(key, default))]
+        # "gemm_split_tail" named an earlier, slower split of the last wave;
+        # plans that carry it take the stream-K default.
+        blob.pop("gemm_split_tail", None)
         fields = Plan.__dataclass_fields__.keys()
         return Plan(**{k: v for k, v in blob.items() if k in fields})
 
@@ -161,8 +164,8 @@ def select_plan(batch: int, seq: int, d_model: int, heads: int, ffn_dim: int, la
         plan = replace(plan, skip_padding=False)
     if os.environ.get("TJ_ATTN_STATIC") == "1":
         plan = replace(plan, attn_dynamic=False)
-    if os.environ.get("TJ_SPLIT_TAIL") == "1":
-        plan = replace(plan, gemm_split_tail=True)
+    if os.environ.get("TJ_NO_STREAM_K") == "1":
+        plan = replace(plan, gemm_stream_k=False)
     forced = os.environ.get("TJ_DELTA_DTYPE")
     if forced in _DTYPES:
         plan = replace(plan, delta_dtype=_DTYPES[forced])
