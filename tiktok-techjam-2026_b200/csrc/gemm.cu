@@ -73,6 +73,15 @@ struct GemmArgs {
 // for long tiles (K = 4096 with one tile in twelve left over: 48 -> 41 us)
 // and loses for K = 1024 or a last wave more than a quarter full.
 constexpr int kSkMinKBlocks = 48;
+// Small-M form: at most one tile per kSkSmallTiles CTAs and K of at least
+// kSkSmallMinKBlocks k-blocks; each tile's k-blocks go over up to
+// kSkSmallRuns runs (its owner adds up to kSkSmallRuns - 1 partials).
+// Measured: M=64 N=768 K=3072 13.6 -> 12.1 us, M=128 N=1024 K=4096 17.0 ->
+// 12.9 us; with eight runs, or with K = 768 (three k-blocks a run), the
+// owner's additions cost more than the spread saves.
+constexpr int kSkSmallTiles = 4;
+constexpr int kSkSmallRuns = 4;
+constexpr int kSkSmallMinKBlocks = 32;
 constexpr int kSkMaxPartials = 160;  // workspace slots: one per CTA, >= grid
 constexpr size_t kSkPartialBytes = static_cast<size_t>(kSkMaxPartials) * kBM * 256 * 4;
 
@@ -223,13 +232,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int grid = static_cast<int>(gridDim.x);
   bool sk = false;
   int sk_w = 0;  // k-blocks per CTA run
-  if (args.ws != nullptr && grid <= kSkMaxPartials && num_k >= kSkMinKBlocks) {
+  if (args.ws != nullptr && grid <= kSkMaxPartials) {
     const int rem = num_tiles % grid;
-    // A last wave at most a quarter full, and at least half a tile per CTA
-    // (so a tile is split over at most three runs).
-    if (rem != 0 && 4 * (grid - rem) >= 3 * grid && 2 * num_tiles >= grid) {
+    if (num_k >= kSkMinKBlocks && rem != 0 && 4 * (grid - rem) >= 3 * grid &&
+        2 * num_tiles >= grid) {
+      // A last wave at most a quarter full, and at least half a tile per CTA
+      // (so a tile is split over at most three runs).
       sk = true;
       sk_w = (num_tiles * num_k + grid - 1) / grid;
+    } else if (kSkSmallTiles * num_tiles <= grid && num_k >= kSkSmallMinKBlocks) {
+      // Few tiles (small M): spread each tile's k-blocks over up to
+      // kSkSmallRuns CTAs, so that many SMs stream the weights at once.
+      sk = true;
+      sk_w = max((num_tiles * num_k + grid - 1) / grid, (num_k + kSkSmallRuns - 1) / kSkSmallRuns);
     }
   }
   auto pieces = [&]() {
@@ -511,7 +526,12 @@ int launch_gemm(const void* A, const void* B, const GemmArgs& args, int lda, int
                     static_cast<uint32_t>(128 / esz), 32);
   if (st != TJB_OK) return st;
   const int num_tiles = ((args.M + kBM - 1) / kBM) * ((args.N + BN - 1) / BN);
-  const int grid = num_tiles < num_sms() ? num_tiles : num_sms();
+  int grid = num_tiles < num_sms() ? num_tiles : num_sms();
+  // Few tiles with a stream-K workspace: launch a CTA per SM (up to the
+  // workspace's slots) so the kernel can spread the k-blocks.
+  if (args.ws != nullptr && kSkSmallTiles * num_tiles <= num_sms() &&
+      (args.K + kBK - 1) / kBK >= kSkSmallMinKBlocks)
+    grid = num_sms() < kSkMaxPartials ? num_sms() : kSkMaxPartials;
   return launch_kernel(gemm_kernel<BN>, dim3(grid), dim3(kGemmThreads), Cfg::kSmemBytes, stream,
                        tmA, tmB, tmC, args);
 }
@@ -561,10 +581,13 @@ int gemm_impl(const void* A, const void* B, const float* bias, void* C, int M, i
   // live-tile list the listed count is not known on the host, so M is taken
   // as given.
   // With a stream-K workspace a partial last wave costs only its share of the
-  // k-blocks, so the widest (most efficient) tile wins whenever N allows it.
+  // k-blocks, so the widest (most efficient) tile wins whenever the kernel
+  // can use stream-K (long K, at least half a 256-wide tile per SM; with a
+  // live-tile list M is an upper bound and the kernel decides again).
   const long mt = (M + kBM - 1) / kBM;
   auto waves = [&](int bn) { return (mt * ((N + bn - 1) / bn) + sms - 1) / sms; };
-  if (workspace != nullptr && N >= 256 && (K + kBK - 1) / kBK >= kSkMinKBlocks) {
+  if (workspace != nullptr && N >= 256 && (K + kBK - 1) / kBK >= kSkMinKBlocks &&
+      2 * mt * ((N + 255) / 256) >= sms) {
     args.idesc = idesc_f16(kBM, 256, bf16, false);
     return launch_gemm<256>(A, B, args, lda, ldb, bf16, s);
   }
