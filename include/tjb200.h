@@ -123,8 +123,9 @@ size_t tjb_gemm_workspace_bytes(void);
 /*
  * tjb_gemm_bias_tiles with stream-K: when K spans at least 48 k-blocks of 64
  * and the last wave of output tiles would leave at least three quarters of
- * the SMs idle, the tiles' k-blocks are divided into one equal run per CTA;
- * a tile whose k-blocks fall into two or three runs has its partial sums
+ * the SMs idle (or, for long K, when there is at most one tile per four
+ * SMs), the tiles' k-blocks are divided into equal runs, one per CTA; a
+ * tile whose k-blocks fall into two to four runs has its partial sums
  * (fp32) meet in the workspace, added by the CTA holding its first k-block.
  * Other shapes run as tjb_gemm_bias_tiles.  workspace: tjb_gemm_workspace_bytes()
  * bytes of device memory, 16-byte aligned, zero-filled before its first use;

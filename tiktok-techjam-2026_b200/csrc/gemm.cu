@@ -55,7 +55,9 @@ struct GemmArgs {
   uint32_t idesc;
   // Split-K tail workspace (null: every tile is computed whole by one CTA).
   float* ws;      // [kSkMaxPartials][kBM][256] fp32 partial tiles
-  int* ws_flags;  // [kSkMaxPartials] arrival counts, zero between launches
+  // [2][kSkMaxPartials]: per contributor slot, the arrivals of its eight
+  // epilogue warps, then the owner warps done reading it; zero between launches.
+  int* ws_flags;
 };
 
 // Stream-K.  When the output tiles do not fill a whole number of waves over
@@ -460,11 +462,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       if (owner) {
-        // This warp has read its share of every partial: give one count back
-        // per contributor (the owner's eight warps return all eight).
+        // This warp has read its share of every partial.  The last of the
+        // owner's eight warps to get here zeroes the slot's counters: every
+        // owner warp has passed its wait by then, so none can miss the
+        // arrivals (returning them one warp at a time could hide them from a
+        // warp still waiting).
         __syncwarp();
         if (lane == 0)
-          for (int c = blockIdx.x + 1; c <= c_last; ++c) atomicSub(args.ws_flags + c, 1);
+          for (int c = blockIdx.x + 1; c <= c_last; ++c)
+            if (atomicAdd(args.ws_flags + kSkMaxPartials + c, 1) == 7) {
+              atomicExch(args.ws_flags + c, 0);
+              atomicExch(args.ws_flags + kSkMaxPartials + c, 0);
+            }
       }
       tc_fence_before();
       __syncwarp();
@@ -609,7 +618,7 @@ int gemm_impl(const void* A, const void* B, const float* bias, void* C, int M, i
 }  // namespace tjb
 
 extern "C" size_t tjb_gemm_workspace_bytes(void) {
-  return tjb::kSkPartialBytes + 256 * sizeof(int);
+  return tjb::kSkPartialBytes + 2 * tjb::kSkMaxPartials * sizeof(int);
 }
 
 extern "C" int tjb_gemm_bias_tiles(const void* A, const void* B, const float* bias, void* C,
