@@ -510,7 +510,10 @@ def main():
         kern = timer.summary(ksteps)
         plans.set_override(None)
 
-    step_max, e2e_max, sg_max = max_over_ranks([step_ms, e2e_ms, sg_ms])
+    status_local = float(K.device_status(clear=True))  # synchronises; after all timing
+    step_max, e2e_max, sg_max, status_max = max_over_ranks([step_ms, e2e_ms, sg_ms,
+                                                            status_local])
+    device_status = int(status_max)
     launches_per_step = sum(v["launches_per_step"] for v in kern.values())
 
     if rank == 0:
@@ -558,6 +561,9 @@ def main():
                                "L2 flush between forwards included"},
             "gpu_launches": int(round(launches_per_step * args.steps)),
             "clocks": clocks.summary(),
+            # Sticky device status word: nonzero if any kernel's bounded wait
+            # ran out during the run (the numbers are then not valid).
+            "device_status": device_status,
         }
         if world > 1 and not tp:
             line["scatter_gather"] = {
@@ -565,6 +571,10 @@ def main():
                 "bytes_per_step": 2 * (world - 1) * b * s * d * 4,
                 "note": "inputs start on GPU 0; per step NCCL scatter of the shards and "
                         "gather of the outputs, max over ranks"}
+        if device_status != 0:
+            print(json.dumps(line), flush=True)
+            raise SystemExit(f"a kernel recorded device status {device_status} "
+                             "(bounded wait ran out): run invalid")
         if world == 1 and not args.no_cpu_baseline:
             sb, sl, calls = cpu_sample_plan(args.config)
             rate, info = cpu_forward_rate(args.config, sb, sl, calls)
