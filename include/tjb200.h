@@ -122,9 +122,10 @@ size_t tjb_gemm_workspace_bytes(void);
 
 /*
  * tjb_gemm_bias_tiles with stream-K: when K spans at least 48 k-blocks of 64
- * and the last wave of output tiles would leave at least three quarters of
- * the SMs idle (or, for long K, when there is at most one tile per four
- * SMs), the tiles' k-blocks are divided into equal runs, one per CTA; a
+ * and the output tiles make at most two waves, the last of which would leave
+ * at least three quarters of the SMs idle (or when there is at most one tile
+ * per four SMs and K spans at least 32 k-blocks), the tiles' k-blocks are
+ * divided into equal runs, one per CTA; a
  * tile whose k-blocks fall into two to four runs has its partial sums
  * (fp32) meet in the workspace, added by the CTA holding its first k-block.
  * Other shapes run as tjb_gemm_bias_tiles.  workspace: tjb_gemm_workspace_bytes()

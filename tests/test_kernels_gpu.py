@@ -89,10 +89,11 @@ def test_gemm_bias(m, n, k, dtype):
     assert ((out16.double() - ref).abs() <= tol * ref.abs() + 1e-3 * scale).all()
 
 
-# Stream-K runs for (5120, 1024, 4096), (5376, 1024, 3072), (9600, 1024, 4096)
-# and (4480, 1032, 4096) (a partial last column tile); its small-M form for
-# (64, 768, 3072), (128, 1024, 4096) and (100, 200, 2048); the other shapes
-# take the whole-tile path with a workspace passed.
+# Stream-K runs for (5120, 1024, 4096), (5376, 1024, 3072) and (4480, 1032,
+# 4096) (a partial last column tile); its small-M form for (64, 768, 3072),
+# (128, 1024, 4096) and (100, 200, 2048); the other shapes (among them
+# (9600, 1024, 4096): more than two waves) take the whole-tile path with a
+# workspace passed.
 SPLIT_SHAPES = [(5120, 1024, 1024), (5120, 1024, 4096), (5376, 1024, 3072), (9600, 1024, 4096),
                 (4480, 1032, 4096), (64, 768, 3072), (128, 1024, 4096), (100, 200, 2048),
                 (4608, 3072, 1024), (300, 136, 512), (2000, 1032, 2048), (129, 64, 64)]

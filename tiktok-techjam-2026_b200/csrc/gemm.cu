@@ -237,9 +237,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (args.ws != nullptr && grid <= kSkMaxPartials) {
     const int rem = num_tiles % grid;
     if (num_k >= kSkMinKBlocks && rem != 0 && 4 * (grid - rem) >= 3 * grid &&
-        2 * num_tiles >= grid) {
-      // A last wave at most a quarter full, and at least half a tile per CTA
-      // (so a tile is split over at most three runs).
+        2 * num_tiles >= grid && num_tiles < 2 * grid) {
+      // A last wave at most a quarter full, at most two waves (beyond that
+      // the idle tail is a small share and every split costs; config 4's
+      // 11-wave GEMMs ran 28% slower with it), and at least half a tile per
+      // CTA (so a tile is split over at most three runs).
       sk = true;
       sk_w = (num_tiles * num_k + grid - 1) / grid;
     } else if (kSkSmallTiles * num_tiles <= grid && num_k >= kSkSmallMinKBlocks) {
@@ -596,7 +598,7 @@ int gemm_impl(const void* A, const void* B, const float* bias, void* C, int M, i
   const long mt = (M + kBM - 1) / kBM;
   auto waves = [&](int bn) { return (mt * ((N + bn - 1) / bn) + sms - 1) / sms; };
   if (workspace != nullptr && N >= 256 && (K + kBK - 1) / kBK >= kSkMinKBlocks &&
-      2 * mt * ((N + 255) / 256) >= sms) {
+      2 * mt * ((N + 255) / 256) >= sms && mt * ((N + 255) / 256) < 2 * sms) {
     args.idesc = idesc_f16(kBM, 256, bf16, false);
     return launch_gemm<256>(A, B, args, lda, ldb, bf16, s);
   }
