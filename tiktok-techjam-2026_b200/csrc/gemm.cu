@@ -15,9 +15,12 @@
 //               buffer back to the MMA warp.  Eight warps rather than four:
 //               the GELU epilogue of the FFN's first GEMM is issue-bound.
 // The epilogue of tile i overlaps the main loop of tile i+1.  With a list of
-// live M tiles (padding-aware forward), only those row tiles are visited.  Output tiles are
-// visited in groups of 16 M-blocks so the CTAs resident at one time share
-// both A rows and B columns in L2.
+// live M tiles (padding-aware forward), only those row tiles are visited.
+// Output tiles are visited in groups of 16 M-blocks so the CTAs resident at
+// one time share both A rows and B columns in L2.  With a caller workspace,
+// GEMMs whose tiles fill the SMs badly run stream-K (see kSkMinKBlocks): each
+// CTA takes an equal run of the tile-major k-block space and split tiles meet
+// in the workspace.
 #include <mutex>
 
 #include "common.cuh"
