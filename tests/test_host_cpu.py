@@ -82,12 +82,26 @@ def test_plan_roundtrip_and_env(tmp_path, monkeypatch):
     monkeypatch.setenv("TJ_COMPUTE_DTYPE", "bfloat16")
     forced = plans.select_plan(2, 128, 512, 8, 2048, 4, True, torch.float32, dev)
     assert not forced.cuda_graph and forced.compute_dtype == torch.bfloat16
+    monkeypatch.setenv("TJ_NO_STREAM_K", "1")
+    assert not plans.select_plan(2, 128, 512, 8, 2048, 4, True, torch.float32, dev).gemm_stream_k
     plans.set_override(p)
     try:
         assert plans.select_plan(1, 1, 1, 1, 1, 1, True, torch.float32, dev) is p
     finally:
         plans.set_override(None)
         plans._cache = None
+
+
+def test_plan_json_from_earlier_builds():
+    """A plan stored before stream-K (with the retired split-tail key) loads
+    with the stream-K default instead of failing."""
+    from tjkernels import plans
+    old = {"compute_dtype": "float16", "residual_dtype": "float32", "delta_dtype": "float16",
+           "cuda_graph": True, "skip_padding": True, "ffn_single_kernel": False,
+           "attn_dynamic": True, "gemm_split_tail": False, "label": "tuned"}
+    p = plans.Plan.from_json(old)
+    assert p.gemm_stream_k and p.label == "tuned" and p.delta_dtype == torch.float16
+    assert "gemm_split_tail" not in p.to_json() and p.to_json()["gemm_stream_k"] is True
 
 
 def test_no_cpu_fallback():
