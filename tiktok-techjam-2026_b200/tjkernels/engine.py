@@ -63,6 +63,25 @@ class LayerWeights:
     b2: torch.Tensor     # [d] fp32
 
 
+def padded_head_dim(hd: int) -> int:
+    """The head_dim the attention kernel runs a head of ``hd`` at: 64 or 128
+    (heads past 128 are left as they are and rejected by the kernel)."""
+    if hd <= 64:
+        return 64
+    if hd <= 128:
+        return 128
+    return hd
+
+
+def pad_heads(t: torch.Tensor, width: int, dim: int) -> torch.Tensor:
+    """Zero-pad dimension ``dim`` of ``t`` (one head's features) to ``width``."""
+    if t.shape[dim] == width:
+        return t
+    shape = list(t.shape)
+    shape[dim] = width - t.shape[dim]
+    return torch.cat([t, t.new_zeros(shape)], dim=dim)
+
+
 class Engine:
     def __init__(self, module: torch.nn.Module) -> None:
         cfg = module.config
@@ -76,6 +95,13 @@ class Engine:
         self.num_layers = cfg.num_layers
         self.causal = cfg.causal
         self.scale = self.head_dim ** -0.5
+        # The attention kernel runs head_dim 64 or 128.  A smaller head (the
+        # reference's d=128/H=4 correctness shape has 32), or one between 64
+        # and 128, is stored zero-padded to the next of the two: the padded
+        # Q/K columns add nothing to the scores, the padded V columns make
+        # zero context columns, and the out-projection ignores them (zero
+        # weight columns); the softmax scale stays 1/sqrt(real head_dim).
+        self.head_dim_run = padded_head_dim(self.head_dim)
 
         self.plan: Optional[Plan] = None
         self._plan_cache: Dict[Tuple[int, int], Plan] = {}
@@ -106,20 +132,27 @@ class Engine:
         if self._tp is not None:
             self._build_tp(plan)
             return
+        heads, hd, hdr = self.num_heads, self.head_dim, self.head_dim_run
         with torch.no_grad():
             for block in self._module.layers:
                 attn = block.attention
                 wqkv = torch.cat([attn.q_proj.weight, attn.k_proj.weight, attn.v_proj.weight],
-                                 dim=0).to(cdt).contiguous()
-                bqkv = torch.cat([attn.q_proj.bias, attn.k_proj.bias, attn.v_proj.bias],
-                                 dim=0).float().contiguous()
+                                 dim=0)
+                bqkv = torch.cat([attn.q_proj.bias, attn.k_proj.bias, attn.v_proj.bias], dim=0)
+                wo = attn.out_proj.weight
+                if hdr != hd:
+                    wqkv = pad_heads(wqkv.view(3 * heads, hd, -1), hdr, dim=1).reshape(
+                        3 * heads * hdr, -1)
+                    bqkv = pad_heads(bqkv.view(3 * heads, hd), hdr, dim=1).reshape(-1)
+                    wo = pad_heads(wo.view(wo.shape[0], heads, hd), hdr, dim=2).reshape(
+                        wo.shape[0], heads * hdr)
                 layers.append(LayerWeights(
                     ln1_w=block.norm1.weight.float().contiguous(),
                     ln1_b=block.norm1.bias.float().contiguous(),
                     ln1_eps=block.norm1.eps,
-                    wqkv=wqkv,
-                    bqkv=bqkv,
-                    wo=attn.out_proj.weight.to(cdt).contiguous(),
+                    wqkv=wqkv.to(cdt).contiguous(),
+                    bqkv=bqkv.float().contiguous(),
+                    wo=wo.to(cdt).contiguous(),
                     bo=attn.out_proj.bias.float().contiguous(),
                     ln2_w=block.norm2.weight.float().contiguous(),
                     ln2_b=block.norm2.bias.float().contiguous(),
@@ -144,6 +177,8 @@ class Engine:
         from .parallel import tp_shard
 
         _, rank, world = self._tp
+        if self.head_dim_run != self.head_dim:
+            raise RuntimeError("tensor parallelism needs head_dim 64 or 128")
         cdt = plan.compute_dtype
         layers: List[LayerWeights] = []
         with torch.no_grad():
@@ -182,7 +217,7 @@ class Engine:
         assert plan is not None and self.final_ln is not None
         batch, seq, d = x.shape
         tokens = batch * seq
-        heads, hd = self.num_heads, self.head_dim
+        heads, hd = self.num_heads, self.head_dim_run
         tp_on = self._tp is not None  # (the group itself may be None: the world)
         tp_group = None
         if tp_on:
