@@ -326,7 +326,8 @@ def workload_config(cfg_id, world, tp=False):
         return {"workload": CONFIG_NOTE[cfg_id] + f" over {world} GPUs", "global_batch": b,
                 "seq_len": s, "d_model": d, "heads": h, "ffn_dim": f, "layers": layers,
                 "parallelism": f"tp{world}: heads and FFN columns split, NCCL all-reduce "
-                               "(fp32) after the out-projection and FFN-out",
+                               "of the partial sums (in the plan's delta dtype) after the "
+                               "out-projection and FFN-out",
                 "l2": "flushed between timed steps (256 MiB write, untimed)"}
     return {"workload": CONFIG_NOTE[cfg_id] + " per GPU", "global_batch": b * world,
             "seq_len": s, "d_model": d, "heads": h, "ffn_dim": f, "layers": layers,

@@ -50,5 +50,6 @@ def test_tensor_parallel_two_gpus():
     for p in procs:
         p.join(timeout=60)
     for rank, usage, zero in results:
+        print(f"tensor parallel rank {rank}: budget usage {usage:.3f}")
         assert usage <= 1.0, (rank, usage)
         assert zero

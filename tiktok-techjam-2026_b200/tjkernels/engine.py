@@ -237,9 +237,10 @@ class Engine:
         if res.dtype != torch.float32 or not res.is_contiguous():
             res = res.float().contiguous()
         own_res = res.data_ptr() != x.data_ptr()
+        # With tensor parallelism the deltas are the per-rank partial sums the
+        # all-reduce adds; they travel in the delta dtype too (16-bit by
+        # default: half the bytes of fp32 on NVLink).
         delta_dtype = torch.float32 if plan.delta_dtype == torch.float32 else plan.compute_dtype
-        if tp_on:
-            delta_dtype = torch.float32  # partial sums are all-reduced in fp32
         ws = self._gemm_ws if plan.gemm_stream_k else None
         pending: Optional[torch.Tensor] = None
         for lw in self.layers:
