@@ -89,6 +89,26 @@ int tjb_add_layernorm_tiles(const float* res, const void* delta, float* res_out,
                             const int32_t* m_tiles, tjb_stream_t stream);
 
 /*
+ * GEMM with the residual add and the following LayerNorm in its epilogue:
+ *   res_out[M, N] = res_in + A[M, K] * W[N, K]^T + bias      (fp32)
+ *   out[M, N]     = LayerNorm(res_out) * gamma + beta         (eps, fp32 stats)
+ * A, W: f16 or bf16 (same type), contiguous (row strides K); res_in,
+ * res_out: fp32 contiguous [M, N] (res_out may equal res_in, or be NULL: not
+ * written); out: f32/f16/bf16 contiguous.  N = 256, 512, 768 or 1024 (one
+ * cluster of N/256 CTAs per 128-row block shares the row statistics through
+ * distributed shared memory), K % 8 == 0.  row_mask (nullable): rows with 0
+ * get a zero output row; m_tiles (nullable) as in tjb_row_tiles.  Replaces the
+ * out-projection / FFN-out torch.addmm and the fused_add_layernorm that
+ * follows it (tjkernels/engine.py:247-256; tjkernels/kernels/__init__.py:48-70)
+ * with one launch in which the GEMM's output never reaches HBM.
+ */
+int tjb_gemm_add_layernorm(const void* A, const void* W, const float* bias, const float* res_in,
+                           float* res_out, const float* gamma, const float* beta, void* out,
+                           int M, int N, int K, float eps, int in_dtype, int out_dtype,
+                           const uint8_t* row_mask, const int32_t* m_tiles,
+                           tjb_stream_t stream);
+
+/*
  * C[M, N] = act(A[M, K] * B[N, K]^T + bias[N])   on tcgen05 tensor cores.
  * A, B: f16 or bf16 (same type), K-major (K contiguous; B is the nn.Linear
  * weight layout [out, in]).  bias: fp32 [N] or NULL.  act: 0 = none,

@@ -161,6 +161,57 @@ def test_gemm_no_bias_and_errors():
         K().gemm_bias(a, torch.randn(60, 64, device=DEV).bfloat16(), None)
 
 
+# ------------------------------------------------------- GEMM + add + LayerNorm
+
+@pytest.mark.parametrize("m,n,k", [(300, 1024, 1024), (129, 256, 512), (1000, 768, 3072),
+                                   (64, 512, 256), (2000, 1024, 4096)])
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
+def test_gemm_add_layernorm(m, n, k, out_dtype):
+    """res + a @ w.T + bias and its LayerNorm in one kernel (row statistics
+    shared over a cluster) against fp64; in place, with a live-tile list and
+    with a row mask."""
+    g = torch.Generator(device=DEV).manual_seed(m + n + k)
+    a = torch.randn(m, k, device=DEV, generator=g).half()
+    w = (torch.randn(n, k, device=DEV, generator=g) / math.sqrt(k)).half()
+    bias = torch.randn(n, device=DEV, generator=g) * 0.1
+    res = torch.randn(m, n, device=DEV, generator=g) * 2 + 0.5
+    gamma = 1 + 0.1 * torch.randn(n, device=DEV, generator=g)
+    beta = 0.1 * torch.randn(n, device=DEV, generator=g)
+    ref_res = res.double() + a.double() @ w.double().T + bias.double()
+    ref = F.layer_norm(ref_res, (n,), gamma.double(), beta.double(), eps=1e-5)
+    res_out, out = K().gemm_add_layernorm(a, w, bias, res, gamma, beta, 1e-5,
+                                          out_dtype=out_dtype)
+    assert (res_out.double() - ref_res).abs().max().item() < 1e-3
+    tol = 4e-3 if out_dtype == torch.float16 else 1e-4
+    assert (out.double() - ref).abs().max().item() < tol
+    # In place, every other 128-row tile live, odd rows masked to zero.
+    n_tiles = (m + 127) // 128
+    live = list(range(0, n_tiles, 2))
+    tiles = torch.tensor([len(live)] + live + [0] * (n_tiles - len(live)), dtype=torch.int32,
+                         device=DEV)
+    row_mask = (torch.arange(m, device=DEV) % 2 == 0).to(torch.uint8)
+    res2 = res.clone()
+    _, out2 = K().gemm_add_layernorm(a, w, bias, res2, gamma, beta, 1e-5, out_dtype=out_dtype,
+                                     residual_out=res2, row_mask=row_mask, m_tiles=tiles)
+    rows = torch.zeros(m, dtype=torch.bool, device=DEV)
+    for t in live:
+        rows[t * 128:(t + 1) * 128] = True
+    assert (res2.double()[rows] - ref_res[rows]).abs().max().item() < 1e-3
+    assert torch.equal(res2[~rows], res[~rows])  # dead tiles untouched
+    keep = rows & row_mask.bool()
+    assert (out2.double()[keep] - ref[keep]).abs().max().item() < tol
+    assert bool((out2[rows & ~row_mask.bool()] == 0).all())
+
+
+def test_gemm_add_layernorm_rejects_unsupported_width():
+    from tjkernels._lib import KernelError
+    a = torch.randn(16, 64, device=DEV).half()
+    w = torch.randn(2048, 64, device=DEV).half()
+    z = torch.zeros(2048, device=DEV)
+    with pytest.raises(KernelError):
+        K().gemm_add_layernorm(a, w, z, torch.zeros(16, 2048, device=DEV), z + 1, z, 1e-5)
+
+
 # ------------------------------------------------------------------ attention
 
 def attn_reference(qkv, causal, lengths=None, key_mask=None):

@@ -181,6 +181,96 @@ __device__ __forceinline__ void stage_row(uint8_t* tile, int r, const uint32_t (
     row[k ^ (r & 7)] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
 }
 
+// Producer role (one thread): TMA-loads the A and B k-blocks of every piece
+// `next` yields into the stage ring; `coords(tile, m_blk, n_blk)` maps a
+// piece's tile to its 128-row block of A and BN-row block of B.  Waits for
+// every load it issued before returning (the CTA may then release memory).
+template <int BN, class Next, class Coords>
+__device__ __forceinline__ void gemm_produce(Next next, Coords coords, const CUtensorMap* tmA,
+                                             const CUtensorMap* tmB, uint8_t* sA, uint8_t* sB,
+                                             uint64_t* full, uint64_t* empty,
+                                             volatile int* abort_flag) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int kStages = Cfg::kStages;
+  int stage = 0;
+  uint32_t phase = 0, issued = 0, issued_parity = 0;
+  bool ok = true;
+  GemmPiece un;
+  while (ok && next(un)) {
+    int m_blk, n_blk;
+    coords(un.tile, m_blk, n_blk);
+    for (int kb = un.kb0; kb < un.kb1; ++kb) {
+      if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
+        ok = false;
+        break;
+      }
+      mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+      tma_load_2d(sA + stage * Cfg::kABytes, tmA, &full[stage], kb * kBK, m_blk * kBM);
+      tma_load_2d(sB + stage * Cfg::kBBytes, tmB, &full[stage], kb * kBK, n_blk * BN);
+      issued |= 1u << stage;
+      issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+      if (++stage == kStages) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+  }
+  for (int s = 0; s < kStages; ++s)
+    if ((issued >> s) & 1u) mbar_wait_drain(&full[s], (issued_parity >> s) & 1u);
+}
+
+// MMA role (one whole warp, converged; one elected lane issues): for every
+// piece `next` yields, accumulate its k-blocks into one of the two TMEM
+// accumulators (BN columns each) and signal tfull; waits for tempty before
+// reusing an accumulator.  Retires every MMA before returning.
+template <int BN, class Next>
+__device__ __forceinline__ void gemm_mma(Next next, uint32_t tmem_base, uint8_t* sA, uint8_t* sB,
+                                         uint64_t* full, uint64_t* empty, uint64_t* tfull,
+                                         uint64_t* tempty, uint64_t* drain, uint32_t idesc,
+                                         volatile int* abort_flag) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int kStages = Cfg::kStages;
+  int stage = 0, acc = 0;
+  uint32_t phase = 0, acc_phase = 0;
+  bool ok = true;
+  auto wait = [&](uint64_t* bar, uint32_t parity) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+  };
+  GemmPiece un;
+  while (ok && next(un)) {
+    if (!wait(&tempty[acc], acc_phase ^ 1)) break;
+    tc_fence_after();
+    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+    for (int kb = un.kb0; kb < un.kb1; ++kb) {
+      if (!wait(&full[stage], phase)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t a0 = smem_u32(sA + stage * Cfg::kABytes);
+      const uint32_t b0 = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+      for (int k = 0; k < kBK / 16; ++k) {
+        umma_ss_w(d_tmem, sdesc_sw128(a0 + k * 32, 16, 1024), sdesc_sw128(b0 + k * 32, 16, 1024),
+                  idesc, (kb > un.kb0 || k > 0) ? 1u : 0u);
+      }
+      umma_commit_w(&empty[stage]);
+      if (++stage == kStages) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+    if (!ok) break;
+    umma_commit_w(&tfull[acc]);
+    if (++acc == 2) {
+      acc = 0;
+      acc_phase ^= 1;
+    }
+  }
+  umma_commit_w(drain);
+  mbar_wait_drain(drain, 0);
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -268,80 +358,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------ producer
-      int stage = 0;
-      uint32_t phase = 0, issued = 0, issued_parity = 0;
-      bool ok = true;
       PieceIter it = pieces();
-      GemmPiece un;
-      while (ok && it.next(un)) {
-        int m_blk, n_blk;
-        tile_coords(un.tile, num_m, num_n, m_blk, n_blk);
-        if (args.m_tiles != nullptr) m_blk = __ldg(args.m_tiles + 1 + m_blk);
-        for (int kb = un.kb0; kb < un.kb1; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-          tma_load_2d(sA + stage * Cfg::kABytes, &tmA, &full[stage], kb * kBK, m_blk * kBM);
-          tma_load_2d(sB + stage * Cfg::kBBytes, &tmB, &full[stage], kb * kBK, n_blk * BN);
-          issued |= 1u << stage;
-          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
-      }
-      // Every load this thread issued has landed before the CTA may exit.
-      for (int s = 0; s < kStages; ++s)
-        if ((issued >> s) & 1u) mbar_wait_drain(&full[s], (issued_parity >> s) & 1u);
+      gemm_produce<BN>([&](GemmPiece& un) { return it.next(un); },
+                       [&](int tile, int& m_blk, int& n_blk) {
+                         tile_coords(tile, num_m, num_n, m_blk, n_blk);
+                         if (args.m_tiles != nullptr) m_blk = __ldg(args.m_tiles + 1 + m_blk);
+                       },
+                       &tmA, &tmB, sA, sB, full, empty, abort_flag);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
-    // The whole warp runs this loop, converged; one elected lane issues.
-    int stage = 0, acc = 0;
-    uint32_t phase = 0, acc_phase = 0;
-    bool ok = true;
-    auto wait = [&](uint64_t* bar, uint32_t parity) {
-      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
-    };
     PieceIter it = pieces();
-    GemmPiece un;
-    while (ok && it.next(un)) {
-      if (!wait(&tempty[acc], acc_phase ^ 1)) break;
-      tc_fence_after();
-      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-      for (int kb = un.kb0; kb < un.kb1; ++kb) {
-        if (!wait(&full[stage], phase)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t a0 = smem_u32(sA + stage * Cfg::kABytes);
-        const uint32_t b0 = smem_u32(sB + stage * Cfg::kBBytes);
-#pragma unroll
-        for (int k = 0; k < kBK / 16; ++k) {
-          umma_ss_w(d_tmem, sdesc_sw128(a0 + k * 32, 16, 1024),
-                    sdesc_sw128(b0 + k * 32, 16, 1024), args.idesc,
-                    (kb > un.kb0 || k > 0) ? 1u : 0u);
-        }
-        umma_commit_w(&empty[stage]);
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1;
-        }
-      }
-      if (!ok) break;
-      umma_commit_w(&tfull[acc]);
-      if (++acc == 2) {
-        acc = 0;
-        acc_phase ^= 1;
-      }
-    }
-    // All issued MMAs retire before tensor memory is released.
-    umma_commit_w(drain);
-    mbar_wait_drain(drain, 0);
+    gemm_mma<BN>([&](GemmPiece& un) { return it.next(un); }, tmem_base, sA, sB, full, empty,
+                 tfull, tempty, drain, args.idesc, abort_flag);
   } else {
     // -------------------------------------------------------------- epilogue
     const int quad = warp & 3;         // TMEM lanes this warp may access

@@ -3,6 +3,7 @@
 #include "runtime.cu"
 #include "layernorm.cu"
 #include "gemm.cu"
+#include "gemm_ln.cu"
 #include "attention.cu"
 #include "ffn.cu"
 #include "ffn_fused.cu"

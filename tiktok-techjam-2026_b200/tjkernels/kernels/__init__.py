@@ -128,8 +128,48 @@ def gemm_bias(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],
     return out
 
 
+def gemm_add_layernorm(a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor,
+                       residual: torch.Tensor, weight: torch.Tensor, ln_bias: torch.Tensor,
+                       eps: float, out_dtype: Optional[torch.dtype] = None,
+                       residual_out: Optional[torch.Tensor] = None, write_residual: bool = True,
+                       row_mask: Optional[torch.Tensor] = None,
+                       m_tiles: Optional[torch.Tensor] = None
+                       ) -> Tuple[Optional[torch.Tensor], torch.Tensor]:
+    """One kernel for ``residual_out = residual + a @ w.T + bias`` (fp32) and
+    ``out = LayerNorm(residual_out) * weight + ln_bias``: the out-projection
+    or FFN-out GEMM with the add+LayerNorm that follows it in a pre-LN block.
+    ``residual_out`` may be ``residual`` (in place); with ``write_residual``
+    False it is not written.  N (= d_model) must be 256, 512, 768 or 1024.
+    Returns ``(residual_out, out)``."""
+    _need_cuda(a, w, bias, residual, weight, ln_bias)
+    m, k = a.shape
+    n, k2 = w.shape
+    if k != k2 or residual.shape != (m, n):
+        raise ValueError("shape mismatch")
+    if a.dtype != w.dtype or residual.dtype != torch.float32:
+        raise TypeError("a and w share a 16-bit dtype; the residual is fp32")
+    for t in (a, w, residual):
+        if not t.is_contiguous():
+            raise ValueError("contiguous tensors only")
+    out_dtype = out_dtype or a.dtype
+    out = torch.empty((m, n), dtype=out_dtype, device=a.device)
+    if write_residual and residual_out is None:
+        residual_out = torch.empty_like(residual)
+    res_out = residual_out if write_residual else None
+    status = _lib.lib().tjb_gemm_add_layernorm(
+        _ptr(a), _ptr(w), _ptr(bias), _ptr(residual), _ptr(res_out), _ptr(weight),
+        _ptr(ln_bias), _ptr(out), m, n, k, float(eps), _code(a.dtype), _code(out_dtype),
+        _ptr(row_mask), _ptr(m_tiles), _stream(a.device))
+    _lib.check(status, "tjb_gemm_add_layernorm")
+    return res_out, out
+
+
+def gemm_add_layernorm_supports(d_model: int) -> bool:
+    return d_model in (256, 512, 768, 1024)
+
+
 def gemm_workspace(device: torch.device) -> torch.Tensor:
-    """A zeroed split-K workspace for :func:`gemm_bias` / :func:`fused_ffn`
+    """A zeroed stream-K workspace for :func:`gemm_bias` / :func:`fused_ffn`
     (``tjb_gemm_workspace_bytes`` bytes); calls that may overlap on the GPU
     need separate workspaces."""
     nbytes = int(_lib.lib().tjb_gemm_workspace_bytes())
@@ -262,6 +302,7 @@ def device_status(clear: bool = False) -> int:
 
 __all__ = [
     "ACT_NONE", "ACT_GELU", "fused_add_layernorm", "layernorm", "gemm_bias", "gemm_workspace",
+    "gemm_add_layernorm", "gemm_add_layernorm_supports",
     "fused_ffn",
     "ffn_single_kernel", "ffn_fused_supports",
     "flash_attention", "flash_supports", "mask_lengths", "row_tiles", "device_status",
