@@ -242,6 +242,10 @@ class Engine:
         # default: half the bytes of fp32 on NVLink).
         delta_dtype = torch.float32 if plan.delta_dtype == torch.float32 else plan.compute_dtype
         ws = self._gemm_ws if plan.gemm_stream_k else None
+        if (plan.fuse_layernorm and not tp_on and K.gemm_add_layernorm_supports(d)
+                and plan.compute_dtype in (torch.float16, torch.bfloat16)):
+            return self._forward_fused_ln(x, res, own_res, tiles, lengths, mask_u8, flags,
+                                          heads, hd, ws).view(batch, seq, d)
         pending: Optional[torch.Tensor] = None
         for lw in self.layers:
             res, h = K.fused_add_layernorm(
@@ -276,6 +280,52 @@ class Engine:
         _, out = K.fused_add_layernorm(res, pending, fw, fb, feps, out_dtype=self.dtype,
                                        write_residual=False, row_mask=mask_u8)
         return out.view(batch, seq, d)
+
+    def _forward_fused_ln(self, x, res, own_res, tiles, lengths, mask_u8, flags, heads, hd,
+                          ws) -> torch.Tensor:
+        """The same block sequence with every LayerNorm after the first one
+        inside the GEMM that produces its input (tjb_gemm_add_layernorm):
+        out-projection -> res += attention out, h2 = LN2(res); FFN-out ->
+        res += FFN out, h = LN1 of the next block (or the final LayerNorm,
+        which writes the output and zeroes padded rows)."""
+        plan = self.plan
+        batch, seq, d = x.shape
+        cdt = plan.compute_dtype
+        layers = self.layers
+        lw0 = layers[0]
+        res, h = K.fused_add_layernorm(res, None, lw0.ln1_w, lw0.ln1_b, lw0.ln1_eps,
+                                       out_dtype=cdt, m_tiles=tiles)
+        out = None
+        for i, lw in enumerate(layers):
+            qkv = K.gemm_bias(h, lw.wqkv, lw.bqkv, m_tiles=tiles, workspace=ws)
+            ctx = K.flash_attention(qkv.view(batch, seq, 3, heads, hd), heads,
+                                    causal=self.causal, lengths=lengths, key_mask=mask_u8,
+                                    mask_flags=flags, scale=self.scale,
+                                    sched=self._attn_sched if plan.attn_dynamic else None)
+            # The first write goes to a fresh buffer unless the residual is
+            # already private (it may be the caller's input).
+            res, h2 = K.gemm_add_layernorm(ctx, lw.wo, lw.bo, res, lw.ln2_w, lw.ln2_b,
+                                           lw.ln2_eps, out_dtype=cdt,
+                                           residual_out=res if own_res else None,
+                                           m_tiles=tiles)
+            own_res = True
+            hidden = K.gemm_bias(h2, lw.w1, lw.b1, act=K.ACT_GELU, m_tiles=tiles, workspace=ws)
+            if i + 1 < len(layers):
+                nxt = layers[i + 1]
+                res, h = K.gemm_add_layernorm(hidden, lw.w2, lw.b2, res, nxt.ln1_w, nxt.ln1_b,
+                                              nxt.ln1_eps, out_dtype=cdt, residual_out=res,
+                                              m_tiles=tiles)
+            else:
+                fw, fb, feps = self.final_ln
+                # Tiles the list skips are all padding: their output rows stay
+                # zero; inside listed tiles the row mask zeroes padded rows.
+                alloc = torch.zeros if tiles is not None else torch.empty
+                _, out = K.gemm_add_layernorm(hidden, lw.w2, lw.b2, res, fw, fb, feps,
+                                              out_dtype=self.dtype, write_residual=False,
+                                              row_mask=mask_u8, m_tiles=tiles,
+                                              out=alloc((batch * seq, d), dtype=self.dtype,
+                                                        device=x.device))
+        return out
 
     # ------------------------------------------------------------------- call
 

@@ -133,7 +133,8 @@ def gemm_add_layernorm(a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor,
                        eps: float, out_dtype: Optional[torch.dtype] = None,
                        residual_out: Optional[torch.Tensor] = None, write_residual: bool = True,
                        row_mask: Optional[torch.Tensor] = None,
-                       m_tiles: Optional[torch.Tensor] = None
+                       m_tiles: Optional[torch.Tensor] = None,
+                       out: Optional[torch.Tensor] = None
                        ) -> Tuple[Optional[torch.Tensor], torch.Tensor]:
     """One kernel for ``residual_out = residual + a @ w.T + bias`` (fp32) and
     ``out = LayerNorm(residual_out) * weight + ln_bias``: the out-projection
@@ -152,7 +153,10 @@ def gemm_add_layernorm(a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor,
         if not t.is_contiguous():
             raise ValueError("contiguous tensors only")
     out_dtype = out_dtype or a.dtype
-    out = torch.empty((m, n), dtype=out_dtype, device=a.device)
+    if out is None:
+        out = torch.empty((m, n), dtype=out_dtype, device=a.device)
+    elif out.shape != (m, n) or out.dtype != out_dtype or not out.is_contiguous():
+        raise ValueError("out must be a contiguous [M, N] tensor of out_dtype")
     if write_residual and residual_out is None:
         residual_out = torch.empty_like(residual)
     res_out = residual_out if write_residual else None

@@ -67,6 +67,14 @@ class Plan:
     # meet in the workspace.  The kernel decides per launch from the live
     # tile count; shapes outside that window run unchanged.
     gemm_stream_k: bool = True
+    # Run the out-projection and FFN-out GEMMs with the residual add and the
+    # next LayerNorm in their epilogue (tjb_gemm_add_layernorm; d_model 256,
+    # 512, 768 or 1024), so their outputs never reach HBM and those
+    # LayerNorms need no pass of their own.  Off by default: measured 9-11 %
+    # slower at configs 2-3 and ~0.1 ms slower at configs 0-1 (clusters of
+    # d/256 CTAs leave SMs of each GPC idle, and the two-pass epilogue with
+    # its cluster exchange sits in the tail of one-to-two-wave GEMMs).
+    fuse_layernorm: bool = False
     label: str = "default"
 
     def to_json(self) -> Dict[str, object]:
@@ -79,6 +87,7 @@ class Plan:
             "ffn_single_kernel": self.ffn_single_kernel,
             "attn_dynamic": self.attn_dynamic,
             "gemm_stream_k": self.gemm_stream_k,
+            "fuse_layernorm": self.fuse_layernorm,
             "label": self.label,
         }
 
@@ -166,6 +175,8 @@ def select_plan(batch: int, seq: int, d_model: int, heads: int, ffn_dim: int, la
         plan = replace(plan, attn_dynamic=False)
     if os.environ.get("TJ_NO_STREAM_K") == "1":
         plan = replace(plan, gemm_stream_k=False)
+    if os.environ.get("TJ_FUSE_LN") == "1":
+        plan = replace(plan, fuse_layernorm=True)
     forced = os.environ.get("TJ_DELTA_DTYPE")
     if forced in _DTYPES:
         plan = replace(plan, delta_dtype=_DTYPES[forced])
