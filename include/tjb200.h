@@ -94,19 +94,25 @@ int tjb_add_layernorm_tiles(const float* res, const void* delta, float* res_out,
  *   out[M, N]     = LayerNorm(res_out) * gamma + beta         (eps, fp32 stats)
  * A, W: f16 or bf16 (same type), contiguous (row strides K); res_in,
  * res_out: fp32 contiguous [M, N] (res_out may equal res_in, or be NULL: not
- * written); out: f32/f16/bf16 contiguous.  N = 256, 512, 768 or 1024 (one
- * cluster of N/256 CTAs per 128-row block shares the row statistics through
- * distributed shared memory), K % 8 == 0.  row_mask (nullable): rows with 0
- * get a zero output row; m_tiles (nullable) as in tjb_row_tiles.  Replaces the
- * out-projection / FFN-out torch.addmm and the fused_add_layernorm that
- * follows it (tjkernels/engine.py:247-256; tjkernels/kernels/__init__.py:48-70)
- * with one launch in which the GEMM's output never reaches HBM.
+ * written); out: f32/f16/bf16 contiguous.  N = 256, 512, 768 or 1024, K % 8
+ * == 0.  The N/256 tiles of a 128-row block exchange per-row (mean, M2)
+ * partials through `workspace` (tjb_gemm_add_layernorm_workspace_bytes(M, N)
+ * bytes, 16-byte aligned, zero before the first call; every call leaves its
+ * counters zero again; calls that may overlap need separate workspaces).
+ * row_mask (nullable): rows with 0 get a zero output row; m_tiles (nullable)
+ * as in tjb_row_tiles.  Replaces the out-projection / FFN-out torch.addmm and
+ * the fused_add_layernorm that follows it (tjkernels/engine.py:247-256;
+ * tjkernels/kernels/__init__.py:48-70) with one launch in which the GEMM's
+ * output never reaches HBM.
  */
 int tjb_gemm_add_layernorm(const void* A, const void* W, const float* bias, const float* res_in,
                            float* res_out, const float* gamma, const float* beta, void* out,
                            int M, int N, int K, float eps, int in_dtype, int out_dtype,
-                           const uint8_t* row_mask, const int32_t* m_tiles,
-                           tjb_stream_t stream);
+                           const uint8_t* row_mask, const int32_t* m_tiles, void* workspace,
+                           size_t workspace_bytes, tjb_stream_t stream);
+
+/* Workspace bytes tjb_gemm_add_layernorm needs for M rows and N columns. */
+size_t tjb_gemm_add_layernorm_workspace_bytes(int M, int N);
 
 /*
  * C[M, N] = act(A[M, K] * B[N, K]^T + bias[N])   on tcgen05 tensor cores.

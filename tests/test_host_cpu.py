@@ -84,11 +84,32 @@ def test_plan_roundtrip_and_env(tmp_path, monkeypatch):
     assert not forced.cuda_graph and forced.compute_dtype == torch.bfloat16
     monkeypatch.setenv("TJ_NO_STREAM_K", "1")
     assert not plans.select_plan(2, 128, 512, 8, 2048, 4, True, torch.float32, dev).gemm_stream_k
+    monkeypatch.setenv("TJ_FUSE_LN", "1")
+    assert plans.select_plan(2, 128, 512, 8, 2048, 4, True, torch.float32, dev).fuse_layernorm
     plans.set_override(p)
     try:
         assert plans.select_plan(1, 1, 1, 1, 1, 1, True, torch.float32, dev) is p
     finally:
         plans.set_override(None)
+        plans._cache = None
+
+
+def test_fused_layernorm_plan_selection(monkeypatch):
+    """The tuned B4 S4096 plan fuses the LayerNorms into the GEMMs, the
+    B8 S1024 one does not; TJ_FUSE_LN=0/1 overrides either way."""
+    from tjkernels import plans
+    dev = torch.device("cuda")
+    monkeypatch.delenv("TJ_IGNORE_PLANS", raising=False)
+    monkeypatch.delenv("TJ_FUSE_LN", raising=False)
+    plans._cache = None
+    try:
+        long_seq = (4, 4096, 1024, 16, 4096, 4, True, torch.float32, dev)
+        assert plans.select_plan(*long_seq).fuse_layernorm
+        assert not plans.select_plan(8, 1024, 1024, 16, 4096, 4, True, torch.float32,
+                                     dev).fuse_layernorm
+        monkeypatch.setenv("TJ_FUSE_LN", "0")
+        assert not plans.select_plan(*long_seq).fuse_layernorm
+    finally:
         plans._cache = None
 
 

@@ -164,12 +164,13 @@ def test_gemm_no_bias_and_errors():
 # ------------------------------------------------------- GEMM + add + LayerNorm
 
 @pytest.mark.parametrize("m,n,k", [(300, 1024, 1024), (129, 256, 512), (1000, 768, 3072),
-                                   (64, 512, 256), (2000, 1024, 4096)])
+                                   (64, 512, 256), (2000, 1024, 4096), (8192, 1024, 1024),
+                                   (9000, 768, 512)])
 @pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
 def test_gemm_add_layernorm(m, n, k, out_dtype):
     """res + a @ w.T + bias and its LayerNorm in one kernel (row statistics
-    shared over a cluster) against fp64; in place, with a live-tile list and
-    with a row mask."""
+    exchanged through a workspace) against fp64; in place, with a live-tile
+    list and with a row mask; the workspace's counters are zero afterwards."""
     g = torch.Generator(device=DEV).manual_seed(m + n + k)
     a = torch.randn(m, k, device=DEV, generator=g).half()
     w = (torch.randn(n, k, device=DEV, generator=g) / math.sqrt(k)).half()
@@ -179,8 +180,9 @@ def test_gemm_add_layernorm(m, n, k, out_dtype):
     beta = 0.1 * torch.randn(n, device=DEV, generator=g)
     ref_res = res.double() + a.double() @ w.double().T + bias.double()
     ref = F.layer_norm(ref_res, (n,), gamma.double(), beta.double(), eps=1e-5)
+    ws = K().gemm_add_layernorm_workspace(m, n, DEV)
     res_out, out = K().gemm_add_layernorm(a, w, bias, res, gamma, beta, 1e-5,
-                                          out_dtype=out_dtype)
+                                          out_dtype=out_dtype, workspace=ws)
     assert (res_out.double() - ref_res).abs().max().item() < 1e-3
     tol = 4e-3 if out_dtype == torch.float16 else 1e-4
     assert (out.double() - ref).abs().max().item() < tol
@@ -192,7 +194,10 @@ def test_gemm_add_layernorm(m, n, k, out_dtype):
     row_mask = (torch.arange(m, device=DEV) % 2 == 0).to(torch.uint8)
     res2 = res.clone()
     _, out2 = K().gemm_add_layernorm(a, w, bias, res2, gamma, beta, 1e-5, out_dtype=out_dtype,
-                                     residual_out=res2, row_mask=row_mask, m_tiles=tiles)
+                                     residual_out=res2, row_mask=row_mask, m_tiles=tiles,
+                                     workspace=ws)
+    counters = ws[:2 * n_tiles * 4].view(torch.int32)
+    assert int(counters.abs().sum().item()) == 0
     rows = torch.zeros(m, dtype=torch.bool, device=DEV)
     for t in live:
         rows[t * 128:(t + 1) * 128] = True

@@ -185,13 +185,12 @@ __device__ __forceinline__ void stage_row(uint8_t* tile, int r, const uint32_t (
 // `next` yields into the stage ring; `coords(tile, m_blk, n_blk)` maps a
 // piece's tile to its 128-row block of A and BN-row block of B.  Waits for
 // every load it issued before returning (the CTA may then release memory).
-template <int BN, class Next, class Coords>
+template <int BN, int kStages = GemmCfg<BN>::kStages, class Next, class Coords>
 __device__ __forceinline__ void gemm_produce(Next next, Coords coords, const CUtensorMap* tmA,
                                              const CUtensorMap* tmB, uint8_t* sA, uint8_t* sB,
                                              uint64_t* full, uint64_t* empty,
                                              volatile int* abort_flag) {
   using Cfg = GemmCfg<BN>;
-  constexpr int kStages = Cfg::kStages;
   int stage = 0;
   uint32_t phase = 0, issued = 0, issued_parity = 0;
   bool ok = true;
@@ -223,13 +222,12 @@ __device__ __forceinline__ void gemm_produce(Next next, Coords coords, const CUt
 // piece `next` yields, accumulate its k-blocks into one of the two TMEM
 // accumulators (BN columns each) and signal tfull; waits for tempty before
 // reusing an accumulator.  Retires every MMA before returning.
-template <int BN, class Next>
+template <int BN, int kStages = GemmCfg<BN>::kStages, class Next>
 __device__ __forceinline__ void gemm_mma(Next next, uint32_t tmem_base, uint8_t* sA, uint8_t* sB,
                                          uint64_t* full, uint64_t* empty, uint64_t* tfull,
                                          uint64_t* tempty, uint64_t* drain, uint32_t idesc,
                                          volatile int* abort_flag) {
   using Cfg = GemmCfg<BN>;
-  constexpr int kStages = Cfg::kStages;
   int stage = 0, acc = 0;
   uint32_t phase = 0, acc_phase = 0;
   bool ok = true;

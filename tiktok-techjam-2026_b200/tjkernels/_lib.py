@@ -49,7 +49,9 @@ SIGNATURES = {
     "tjb_ffn_tiles_ws": (_c_int, [_p, _p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int,
                                   _c_int, _p, _p, ctypes.c_size_t, _p]),
     "tjb_gemm_add_layernorm": (_c_int, [_p, _p, _p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int,
-                                        ctypes.c_float, _c_int, _c_int, _p, _p, _p]),
+                                        ctypes.c_float, _c_int, _c_int, _p, _p, _p,
+                                        ctypes.c_size_t, _p]),
+    "tjb_gemm_add_layernorm_workspace_bytes": (ctypes.c_size_t, [_c_int, _c_int]),
     "tjb_ffn_fused": (_c_int, [_p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int,
                                _p, _p]),
     "tjb_row_tiles": (_c_int, [_p, _p, _c_int, _c_int, _p, _p]),

@@ -119,6 +119,7 @@ class Engine:
         self._attn_sched: Optional[torch.Tensor] = None
         # Split-K workspace of the GEMMs, shared by all of them in order.
         self._gemm_ws: Optional[torch.Tensor] = None
+        self._ln_ws: Optional[torch.Tensor] = None
 
     # ---------------------------------------------------------------- weights
 
@@ -295,6 +296,7 @@ class Engine:
         lw0 = layers[0]
         res, h = K.fused_add_layernorm(res, None, lw0.ln1_w, lw0.ln1_b, lw0.ln1_eps,
                                        out_dtype=cdt, m_tiles=tiles)
+        ln_ws = self._ln_workspace(batch * seq, d, x.device)
         out = None
         for i, lw in enumerate(layers):
             qkv = K.gemm_bias(h, lw.wqkv, lw.bqkv, m_tiles=tiles, workspace=ws)
@@ -307,14 +309,14 @@ class Engine:
             res, h2 = K.gemm_add_layernorm(ctx, lw.wo, lw.bo, res, lw.ln2_w, lw.ln2_b,
                                            lw.ln2_eps, out_dtype=cdt,
                                            residual_out=res if own_res else None,
-                                           m_tiles=tiles)
+                                           m_tiles=tiles, workspace=ln_ws)
             own_res = True
             hidden = K.gemm_bias(h2, lw.w1, lw.b1, act=K.ACT_GELU, m_tiles=tiles, workspace=ws)
             if i + 1 < len(layers):
                 nxt = layers[i + 1]
                 res, h = K.gemm_add_layernorm(hidden, lw.w2, lw.b2, res, nxt.ln1_w, nxt.ln1_b,
                                               nxt.ln1_eps, out_dtype=cdt, residual_out=res,
-                                              m_tiles=tiles)
+                                              m_tiles=tiles, workspace=ln_ws)
             else:
                 fw, fb, feps = self.final_ln
                 # Tiles the list skips are all padding: their output rows stay
@@ -322,10 +324,19 @@ class Engine:
                 alloc = torch.zeros if tiles is not None else torch.empty
                 _, out = K.gemm_add_layernorm(hidden, lw.w2, lw.b2, res, fw, fb, feps,
                                               out_dtype=self.dtype, write_residual=False,
-                                              row_mask=mask_u8, m_tiles=tiles,
+                                              row_mask=mask_u8, m_tiles=tiles, workspace=ln_ws,
                                               out=alloc((batch * seq, d), dtype=self.dtype,
                                                         device=x.device))
         return out
+
+    def _ln_workspace(self, rows: int, d: int, device: torch.device) -> torch.Tensor:
+        """The row-statistics workspace of tjb_gemm_add_layernorm, kept for the
+        largest row count seen (the kernels of one forward run in order)."""
+        ws = self._ln_ws
+        if ws is None or ws.device != device or ws.numel() < K.gemm_add_layernorm_workspace_bytes(
+                rows, d):
+            self._ln_ws = ws = K.gemm_add_layernorm_workspace(rows, d, device)
+        return ws
 
     # ------------------------------------------------------------------- call
 

@@ -134,13 +134,16 @@ def gemm_add_layernorm(a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor,
                        residual_out: Optional[torch.Tensor] = None, write_residual: bool = True,
                        row_mask: Optional[torch.Tensor] = None,
                        m_tiles: Optional[torch.Tensor] = None,
-                       out: Optional[torch.Tensor] = None
+                       out: Optional[torch.Tensor] = None,
+                       workspace: Optional[torch.Tensor] = None
                        ) -> Tuple[Optional[torch.Tensor], torch.Tensor]:
     """One kernel for ``residual_out = residual + a @ w.T + bias`` (fp32) and
     ``out = LayerNorm(residual_out) * weight + ln_bias``: the out-projection
     or FFN-out GEMM with the add+LayerNorm that follows it in a pre-LN block.
     ``residual_out`` may be ``residual`` (in place); with ``write_residual``
     False it is not written.  N (= d_model) must be 256, 512, 768 or 1024.
+    ``workspace`` (see :func:`gemm_add_layernorm_workspace`) carries the row
+    statistics between the tiles of a row block; one is made when it is None.
     Returns ``(residual_out, out)``."""
     _need_cuda(a, w, bias, residual, weight, ln_bias)
     m, k = a.shape
@@ -160,16 +163,31 @@ def gemm_add_layernorm(a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor,
     if write_residual and residual_out is None:
         residual_out = torch.empty_like(residual)
     res_out = residual_out if write_residual else None
+    if workspace is None:
+        workspace = gemm_add_layernorm_workspace(m, n, a.device)
     status = _lib.lib().tjb_gemm_add_layernorm(
         _ptr(a), _ptr(w), _ptr(bias), _ptr(residual), _ptr(res_out), _ptr(weight),
         _ptr(ln_bias), _ptr(out), m, n, k, float(eps), _code(a.dtype), _code(out_dtype),
-        _ptr(row_mask), _ptr(m_tiles), _stream(a.device))
+        _ptr(row_mask), _ptr(m_tiles), _ptr(workspace),
+        workspace.numel() * workspace.element_size(), _stream(a.device))
     _lib.check(status, "tjb_gemm_add_layernorm")
     return res_out, out
 
 
 def gemm_add_layernorm_supports(d_model: int) -> bool:
     return d_model in (256, 512, 768, 1024)
+
+
+def gemm_add_layernorm_workspace(rows: int, d_model: int, device: torch.device) -> torch.Tensor:
+    """A zeroed workspace for :func:`gemm_add_layernorm` on up to ``rows``
+    rows (``tjb_gemm_add_layernorm_workspace_bytes``); calls that may overlap
+    on the GPU need separate workspaces."""
+    return torch.zeros(gemm_add_layernorm_workspace_bytes(rows, d_model), dtype=torch.uint8,
+                       device=device)
+
+
+def gemm_add_layernorm_workspace_bytes(rows: int, d_model: int) -> int:
+    return int(_lib.lib().tjb_gemm_add_layernorm_workspace_bytes(rows, d_model))
 
 
 def gemm_workspace(device: torch.device) -> torch.Tensor:
@@ -306,6 +324,7 @@ def device_status(clear: bool = False) -> int:
 
 __all__ = [
     "ACT_NONE", "ACT_GELU", "fused_add_layernorm", "layernorm", "gemm_bias", "gemm_workspace",
+    "gemm_add_layernorm_workspace", "gemm_add_layernorm_workspace_bytes",
     "gemm_add_layernorm", "gemm_add_layernorm_supports",
     "fused_ffn",
     "ffn_single_kernel", "ffn_fused_supports",

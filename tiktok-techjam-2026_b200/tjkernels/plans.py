@@ -70,10 +70,10 @@ class Plan:
     # Run the out-projection and FFN-out GEMMs with the residual add and the
     # next LayerNorm in their epilogue (tjb_gemm_add_layernorm; d_model 256,
     # 512, 768 or 1024), so their outputs never reach HBM and those
-    # LayerNorms need no pass of their own.  Off by default: measured 9-11 %
-    # slower at configs 2-3 and ~0.1 ms slower at configs 0-1 (clusters of
-    # d/256 CTAs leave SMs of each GPC idle, and the two-pass epilogue with
-    # its cluster exchange sits in the tail of one-to-two-wave GEMMs).
+    # LayerNorms need no pass of their own.  Off by default, on in the tuned
+    # plan of the B4 S4096 shape (1-3 % faster there); slower where the GEMM
+    # has too few 128 x 256 tiles (B1 S64: one row block, three CTAs) or needs
+    # stream-K for its K = 4096 tail wave (B8 S1024: 4 % slower).
     fuse_layernorm: bool = False
     label: str = "default"
 
@@ -175,8 +175,8 @@ def select_plan(batch: int, seq: int, d_model: int, heads: int, ffn_dim: int, la
         plan = replace(plan, attn_dynamic=False)
     if os.environ.get("TJ_NO_STREAM_K") == "1":
         plan = replace(plan, gemm_stream_k=False)
-    if os.environ.get("TJ_FUSE_LN") == "1":
-        plan = replace(plan, fuse_layernorm=True)
+    if os.environ.get("TJ_FUSE_LN") in ("0", "1"):
+        plan = replace(plan, fuse_layernorm=os.environ["TJ_FUSE_LN"] == "1")
     forced = os.environ.get("TJ_DELTA_DTYPE")
     if forced in _DTYPES:
         plan = replace(plan, delta_dtype=_DTYPES[forced])
