@@ -502,7 +502,8 @@ def main():
         ksteps = max(3, min(args.steps, 20))
         # Per-kernel rates come from the unfused form of the plan (each
         # kernel family on its own: GEMMs, attention, FFN, LayerNorm); the
-        # launch count from one eager forward of the plan itself.
+        # launch count and the rates of the plan's own kernels (the fused
+        # GEMM + LayerNorm among them) from eager forwards of the plan itself.
         plans.set_override(plans.Plan(compute_dtype=plan.compute_dtype,
                                       delta_dtype=plan.delta_dtype, cuda_graph=False,
                                       fuse_layernorm=False, label="instrumented"))
@@ -516,10 +517,14 @@ def main():
         kern = timer.summary(ksteps)
         plans.set_override(dataclasses.replace(plan, cuda_graph=False))
         model(x, mask)
+        torch.cuda.synchronize(dev)
         counter = KernelTimer(K, {"lengths": lengths, "valid_tokens": sum(lengths)})
         with counter:
-            model(x, mask)
-        launches_real = sum(v["launches_per_step"] for v in counter.summary(1).values())
+            for _ in range(ksteps):
+                model(x, mask)
+                flush.zero_()
+        kern_plan = counter.summary(ksteps)
+        launches_real = sum(v["launches_per_step"] for v in kern_plan.values())
         plans.set_override(None)
 
     status_local = float(K.device_status(clear=True))  # synchronises; after all timing
@@ -562,10 +567,13 @@ def main():
                 "attn_tflops": attn["tflops"], "attn_frac": attn["tflops"] / peak,
                 "ffn_tflops": kern["fused_ffn"]["tflops"],
                 "ffn_frac": kern["fused_ffn"]["tflops"] / peak,
+                # The plan's fused GEMM + add + LayerNorm (when it runs one).
+                "gemm_ln_tflops": kern_plan.get("gemm_add_layernorm", {}).get("tflops"),
                 "layernorm_gbs": ln["gbs"], "layernorm_frac": ln["gbs"] / peaks["hbm_gbs"],
                 "eager_step_ms": sum(v["ms_per_step"] for v in kern.values()),
             },
             "kernels": kern,
+            "kernels_plan": kern_plan,
             "e2e": {"value": tokens / (e2e_max / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": x_cpu.numel() * 4 + mask_cpu.numel(),
                     "d2h_bytes_per_step": b * s * d * 4, "ms_per_step": e2e_max,

@@ -96,7 +96,7 @@ def test_plan_roundtrip_and_env(tmp_path, monkeypatch):
 
 def test_fused_layernorm_plan_selection(monkeypatch):
     """The tuned B4 S4096 plan fuses the LayerNorms into the GEMMs, the
-    B8 S1024 one does not; TJ_FUSE_LN=0/1 overrides either way."""
+    B8 S1024 one only the out-projection's; TJ_FUSE_LN=0/1 overrides."""
     from tjkernels import plans
     dev = torch.device("cuda")
     monkeypatch.delenv("TJ_IGNORE_PLANS", raising=False)
@@ -104,9 +104,10 @@ def test_fused_layernorm_plan_selection(monkeypatch):
     plans._cache = None
     try:
         long_seq = (4, 4096, 1024, 16, 4096, 4, True, torch.float32, dev)
-        assert plans.select_plan(*long_seq).fuse_layernorm
-        assert not plans.select_plan(8, 1024, 1024, 16, 4096, 4, True, torch.float32,
-                                     dev).fuse_layernorm
+        p3 = plans.select_plan(*long_seq)
+        assert p3.fuse_layernorm and p3.fuse_layernorm_ffn
+        p2 = plans.select_plan(8, 1024, 1024, 16, 4096, 4, True, torch.float32, dev)
+        assert p2.fuse_layernorm and not p2.fuse_layernorm_ffn
         monkeypatch.setenv("TJ_FUSE_LN", "0")
         assert not plans.select_plan(*long_seq).fuse_layernorm
     finally:

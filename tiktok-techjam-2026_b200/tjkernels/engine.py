@@ -284,21 +284,28 @@ class Engine:
 
     def _forward_fused_ln(self, x, res, own_res, tiles, lengths, mask_u8, flags, heads, hd,
                           ws) -> torch.Tensor:
-        """The same block sequence with every LayerNorm after the first one
-        inside the GEMM that produces its input (tjb_gemm_add_layernorm):
-        out-projection -> res += attention out, h2 = LN2(res); FFN-out ->
-        res += FFN out, h = LN1 of the next block (or the final LayerNorm,
-        which writes the output and zeroes padded rows)."""
+        """The same block sequence with LayerNorms inside the GEMM that
+        produces their input (tjb_gemm_add_layernorm): out-projection ->
+        res += attention out, h2 = LN2(res); with ``plan.fuse_layernorm_ffn``
+        also FFN-out -> res += FFN out, h = LN1 of the next block (or the
+        final LayerNorm, which writes the output and zeroes padded rows);
+        without it the FFN runs as in the plain sequence (stream-K GEMMs) and
+        its add+LayerNorm stays a launch of its own."""
         plan = self.plan
         batch, seq, d = x.shape
         cdt = plan.compute_dtype
+        delta_dtype = torch.float32 if plan.delta_dtype == torch.float32 else cdt
         layers = self.layers
         lw0 = layers[0]
         res, h = K.fused_add_layernorm(res, None, lw0.ln1_w, lw0.ln1_b, lw0.ln1_eps,
                                        out_dtype=cdt, m_tiles=tiles)
         ln_ws = self._ln_workspace(batch * seq, d, x.device)
+        pending: Optional[torch.Tensor] = None
         out = None
         for i, lw in enumerate(layers):
+            if pending is not None:
+                res, h = K.fused_add_layernorm(res, pending, lw.ln1_w, lw.ln1_b, lw.ln1_eps,
+                                               out_dtype=cdt, residual_out=res, m_tiles=tiles)
             qkv = K.gemm_bias(h, lw.wqkv, lw.bqkv, m_tiles=tiles, workspace=ws)
             ctx = K.flash_attention(qkv.view(batch, seq, 3, heads, hd), heads,
                                     causal=self.causal, lengths=lengths, key_mask=mask_u8,
@@ -311,6 +318,10 @@ class Engine:
                                            residual_out=res if own_res else None,
                                            m_tiles=tiles, workspace=ln_ws)
             own_res = True
+            if not plan.fuse_layernorm_ffn:
+                pending = K.fused_ffn(h2, lw.w1, lw.b1, lw.w2, lw.b2, out_dtype=delta_dtype,
+                                      m_tiles=tiles, workspace=ws)
+                continue
             hidden = K.gemm_bias(h2, lw.w1, lw.b1, act=K.ACT_GELU, m_tiles=tiles, workspace=ws)
             if i + 1 < len(layers):
                 nxt = layers[i + 1]
@@ -327,6 +338,10 @@ class Engine:
                                               row_mask=mask_u8, m_tiles=tiles, workspace=ln_ws,
                                               out=alloc((batch * seq, d), dtype=self.dtype,
                                                         device=x.device))
+        if pending is not None:
+            fw, fb, feps = self.final_ln
+            _, out = K.fused_add_layernorm(res, pending, fw, fb, feps, out_dtype=self.dtype,
+                                           write_residual=False, row_mask=mask_u8)
         return out
 
     def _ln_workspace(self, rows: int, d: int, device: torch.device) -> torch.Tensor:

@@ -70,11 +70,16 @@ class Plan:
     # Run the out-projection and FFN-out GEMMs with the residual add and the
     # next LayerNorm in their epilogue (tjb_gemm_add_layernorm; d_model 256,
     # 512, 768 or 1024), so their outputs never reach HBM and those
-    # LayerNorms need no pass of their own.  Off by default, on in the tuned
-    # plan of the B4 S4096 shape (1-3 % faster there); slower where the GEMM
-    # has too few 128 x 256 tiles (B1 S64: one row block, three CTAs) or needs
-    # stream-K for its K = 4096 tail wave (B8 S1024: 4 % slower).
+    # LayerNorms need no pass of their own.  Off by default; on in the tuned
+    # plan of the B4 S4096 shape (1-3 % faster there) and, for the
+    # out-projection only, of the B8 S1024 shape (0.7 %; fusing its FFN-out
+    # too is 4 % slower, since that GEMM needs stream-K for its K = 4096
+    # tail wave); slower where the GEMM has too few 128 x 256 tiles (B1 S64:
+    # one row block, three CTAs).
     fuse_layernorm: bool = False
+    # With fuse_layernorm: also fuse the FFN-out GEMM (False keeps it on the
+    # plain GEMM, with stream-K, and a standalone add+LayerNorm after it).
+    fuse_layernorm_ffn: bool = True
     label: str = "default"
 
     def to_json(self) -> Dict[str, object]:
@@ -88,6 +93,7 @@ class Plan:
             "attn_dynamic": self.attn_dynamic,
             "gemm_stream_k": self.gemm_stream_k,
             "fuse_layernorm": self.fuse_layernorm,
+            "fuse_layernorm_ffn": self.fuse_layernorm_ffn,
             "label": self.label,
         }
 
@@ -177,6 +183,8 @@ def select_plan(batch: int, seq: int, d_model: int, heads: int, ffn_dim: int, la
         plan = replace(plan, gemm_stream_k=False)
     if os.environ.get("TJ_FUSE_LN") in ("0", "1"):
         plan = replace(plan, fuse_layernorm=os.environ["TJ_FUSE_LN"] == "1")
+    if os.environ.get("TJ_FUSE_LN_FFN") in ("0", "1"):
+        plan = replace(plan, fuse_layernorm_ffn=os.environ["TJ_FUSE_LN_FFN"] == "1")
     forced = os.environ.get("TJ_DELTA_DTYPE")
     if forced in _DTYPES:
         plan = replace(plan, delta_dtype=_DTYPES[forced])
