@@ -463,12 +463,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             }
           }
         }
-        // Row max: eight independent three-input max chains, then combine.
+        // Row max: eight independent chains over 16-column steps, then combine.
         float pm[8];
 #pragma unroll
-        for (int a = 0; a < 8; ++a) pm[a] = __uint_as_float(sv[a]);
+        for (int a = 0; a < 8; ++a) pm[a] = fmaxf(__uint_as_float(sv[a]), __uint_as_float(sv[8 + a]));
 #pragma unroll
-        for (int c = 8; c < kTileK; c += 16) {
+        for (int c = 16; c < kTileK; c += 16) {
 #pragma unroll
           for (int a = 0; a < 8; ++a)
             pm[a] = fmax3(pm[a], __uint_as_float(sv[c + a]), __uint_as_float(sv[c + 8 + a]));
