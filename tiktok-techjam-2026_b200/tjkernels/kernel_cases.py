@@ -4,6 +4,7 @@
     python -m tjkernels.kernel_cases attn B S H HD [--lengths prefix] [--launches 3]
     python -m tjkernels.kernel_cases ln ROWS D [--launches 3]
     python -m tjkernels.kernel_cases ffn T D F [--launches 3]
+    python -m tjkernels.kernel_cases gemm_ln M N K [--launches 3]
 
 Each call launches the kernel ``--launches`` times (fp16 inputs) and prints
 the median CUDA-event time of all but the first launch.  It is the
@@ -39,7 +40,7 @@ def _timed(fn, launches: int) -> float:
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("kernel", choices=["gemm", "attn", "ln", "ffn"])
+    ap.add_argument("kernel", choices=["gemm", "attn", "ln", "ffn", "gemm_ln"])
     ap.add_argument("dims", type=int, nargs="+")
     ap.add_argument("--act", choices=["none", "gelu"], default="none")
     ap.add_argument("--out", choices=["f16", "f32"], default="f16")
@@ -89,6 +90,20 @@ def main(argv=None) -> int:
                                                   out_dtype=torch.float16, residual_out=res),
                     args.launches)
         flops = 0.0
+    elif args.kernel == "gemm_ln":
+        # GEMM + residual add + LayerNorm in one kernel, residual in place.
+        m, n, k = args.dims
+        a, w = randn(m, k), randn(n, k, scale=k ** -0.5)
+        bias = torch.randn(n, device=dev, generator=g)
+        res = torch.randn(m, n, device=dev, generator=g)
+        gamma = torch.ones(n, device=dev)
+        beta = torch.zeros(n, device=dev)
+        out = torch.empty(m, n, dtype=torch.float16, device=dev)
+        ws = K.gemm_add_layernorm_workspace(m, n, dev)
+        ms = _timed(lambda: K.gemm_add_layernorm(a, w, bias, res, gamma, beta, 1e-5,
+                                                 residual_out=res, out=out, workspace=ws),
+                    args.launches)
+        flops = 2.0 * m * n * k
     else:
         t, d, f = args.dims
         h = randn(t, d)
