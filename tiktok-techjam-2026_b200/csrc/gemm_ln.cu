@@ -50,7 +50,8 @@ struct GemmLnArgs {
 struct GemmLnSmem {
   static constexpr size_t kRing = static_cast<size_t>(kLnStages) * GemmCfg<256>::kStageBytes;
   static constexpr size_t kStaging = 8 * 2 * kLnChunk;  // [warp][buffer]
-  static constexpr size_t kBytes = 1024 + kRing + kStaging + 512;
+  static constexpr size_t kParams = 8 * 3 * 128 * sizeof(float);  // [warp][bias|gamma|beta][128]
+  static constexpr size_t kBytes = 1024 + kRing + kStaging + kParams + 512;
 };
 
 __device__ __forceinline__ void ld_chunk_row(const uint8_t* buf, int r, float (&v)[32]) {
@@ -77,7 +78,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + kLnStages * Cfg::kABytes;
   uint8_t* staging = smem + GemmLnSmem::kRing;  // [warp 0..7][2][kLnChunk]
-  uint64_t* full = reinterpret_cast<uint64_t*>(staging + GemmLnSmem::kStaging);
+  float* params = reinterpret_cast<float*>(staging + GemmLnSmem::kStaging);
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(params) +
+                                               GemmLnSmem::kParams);
   uint64_t* empty = full + kLnStages;
   uint64_t* tfull = empty + kLnStages;
   uint64_t* tempty = tfull + 2;
@@ -155,6 +158,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int quad = warp & 3;         // TMEM lanes this warp may access
     const int half = (warp - 2) >> 2;  // which 128 of the tile's 256 columns
     uint8_t* const buf0 = staging + ew * 2 * kLnChunk;
+    // This warp's 128 columns of bias, gamma and beta, staged once per tile
+    // (every lane reads every column: shared-memory broadcasts).
+    float* const prm = params + ew * 3 * 128;
     auto buf = [&](int b) { return buf0 + b * kLnChunk; };
     auto bar = [&](int b) { return &rbar[ew * 2 + b]; };
     uint32_t bar_phase = 0;  // bit b: parity of buffer b's next load
@@ -195,8 +201,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (lane == 0) bulk_wait_read<0>();
       __syncwarp();
       load_res(0, col0, row0);
+      // Column parameters and the row mask: loads issued before the wait
+      // for the accumulator so that their latency hides behind it.
+      float4 pv[3];
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        const float* src = k == 0 ? args.bias : k == 1 ? args.gamma : args.beta;
+        pv[k] = __ldg(reinterpret_cast<const float4*>(src + col0) + lane);
+      }
+      const bool zero_row = args.row_mask != nullptr && valid && args.row_mask[row] == 0;
       if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, abort_flag))) break;
       tc_fence_after();
+#pragma unroll
+      for (int k = 0; k < 3; ++k) reinterpret_cast<float4*>(prm + k * 128)[lane] = pv[k];
+      __syncwarp();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * 256 + half * 128);
       // Pass 1: v = acc + bias + residual, back into the accumulator; this
@@ -215,12 +233,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         float x[32];
         ld_chunk_row(buf(c & 1), lane, x);
         __syncwarp();  // every lane has read the buffer before it is refilled
-        const float4* b4 = reinterpret_cast<const float4*>(args.bias + col0 + c * 32);
+        const float4* b4 = reinterpret_cast<const float4*>(prm + c * 32);
         float v[32];
         float sum = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const float4 bb = __ldg(b4 + i);
+          const float4 bb = b4[i];
           v[4 * i] = __uint_as_float(r[4 * i]) + bb.x + x[4 * i];
           v[4 * i + 1] = __uint_as_float(r[4 * i + 1]) + bb.y + x[4 * i + 1];
           v[4 * i + 2] = __uint_as_float(r[4 * i + 2]) + bb.z + x[4 * i + 2];
@@ -284,7 +302,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         atomicExch(readers, 0);
       }
       // Pass 2: normalise; stage and store the residual and the output.
-      const bool zero_row = args.row_mask != nullptr && valid && args.row_mask[row] == 0;
       int sb = 0;  // staging buffer for the next store
 #pragma unroll 1
       for (int c = 0; c < 4; c += out_cols / 32) {
@@ -306,13 +323,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             sb ^= 1;
           }
-          const float4* g4 = reinterpret_cast<const float4*>(args.gamma + col);
-          const float4* e4 = reinterpret_cast<const float4*>(args.beta + col);
+          const float4* g4 = reinterpret_cast<const float4*>(prm + 128 + (c + cc) * 32);
+          const float4* e4 = reinterpret_cast<const float4*>(prm + 256 + (c + cc) * 32);
           float y[32];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            const float4 gg = __ldg(g4 + i);
-            const float4 bb = __ldg(e4 + i);
+            const float4 gg = g4[i];
+            const float4 bb = e4[i];
             y[4 * i] = (__uint_as_float(r[4 * i]) - mu) * rstd * gg.x + bb.x;
             y[4 * i + 1] = (__uint_as_float(r[4 * i + 1]) - mu) * rstd * gg.y + bb.y;
             y[4 * i + 2] = (__uint_as_float(r[4 * i + 2]) - mu) * rstd * gg.z + bb.z;
