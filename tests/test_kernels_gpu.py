@@ -208,6 +208,25 @@ def test_gemm_add_layernorm(m, n, k, out_dtype):
     assert bool((out2[rows & ~row_mask.bool()] == 0).all())
 
 
+@pytest.mark.parametrize("m,n,k", [(300, 1024, 1024), (9000, 768, 512)])
+def test_gemm_add_layernorm_bf16(m, n, k):
+    """The bf16-operand form of the fused GEMM + add + LayerNorm against
+    fp64 (bf16 output)."""
+    g = torch.Generator(device=DEV).manual_seed(7 * m + n)
+    a = torch.randn(m, k, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(n, k, device=DEV, generator=g) / math.sqrt(k)).bfloat16()
+    bias = torch.randn(n, device=DEV, generator=g) * 0.1
+    res = torch.randn(m, n, device=DEV, generator=g)
+    gamma = 1 + 0.1 * torch.randn(n, device=DEV, generator=g)
+    beta = 0.1 * torch.randn(n, device=DEV, generator=g)
+    ref_res = res.double() + a.double() @ w.double().T + bias.double()
+    ref = F.layer_norm(ref_res, (n,), gamma.double(), beta.double(), eps=1e-5)
+    res_out, out = K().gemm_add_layernorm(a, w, bias, res, gamma, beta, 1e-5)
+    assert out.dtype == torch.bfloat16
+    assert (res_out.double() - ref_res).abs().max().item() < 1e-3
+    assert (out.double() - ref).abs().max().item() < 3e-2  # bf16 output rounding
+
+
 def test_gemm_add_layernorm_rejects_unsupported_width():
     from tjkernels._lib import KernelError
     a = torch.randn(16, 64, device=DEV).half()
