@@ -75,8 +75,9 @@ int hidden_address(void** out) {
   std::lock_guard<std::mutex> lock(g_hidden_mu);
   if (g_hidden_addr[dev] == nullptr) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_ffn_hidden) != cudaSuccess || p == nullptr)
-      return TJB_ERR_LAUNCH;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_ffn_hidden);
+    if (e != cudaSuccess) return cuda_status(e);  // recorded for tjb_last_cuda_error
+    if (p == nullptr) return TJB_ERR_LAUNCH;
     g_hidden_addr[dev] = p;
   }
   *out = g_hidden_addr[dev];
