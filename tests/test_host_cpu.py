@@ -114,6 +114,27 @@ def test_fused_layernorm_plan_selection(monkeypatch):
         plans._cache = None
 
 
+def test_layernorm_workspace_outlives_the_graphs_that_use_it(monkeypatch):
+    """When a larger batch grows the fused LayerNorm's workspace, the old one
+    stays alive (graphs captured for the smaller shape still point at it)
+    until the engine releases its graphs."""
+    from tjkernels import engine as E
+    from tjkernels import kernels as K
+    monkeypatch.setattr(K, "gemm_add_layernorm_workspace",
+                        lambda rows, d, device: torch.zeros(
+                            K.gemm_add_layernorm_workspace_bytes(rows, d), dtype=torch.uint8))
+    eng = E.Engine.__new__(E.Engine)
+    eng._ln_ws = None
+    eng._ln_ws_retired = []
+    cpu = torch.device("cpu")
+    small = eng._ln_workspace(1024, 1024, cpu)
+    assert eng._ln_workspace(512, 1024, cpu) is small  # fits: reused
+    big = eng._ln_workspace(8192, 1024, cpu)
+    assert big is not small and big.numel() > small.numel()
+    assert any(t is small for t in eng._ln_ws_retired)
+    assert eng._ln_workspace(8192, 1024, cpu) is big
+
+
 def test_plan_json_from_earlier_builds():
     """A plan stored before stream-K (with the retired split-tail key) loads
     with the stream-K default instead of failing."""

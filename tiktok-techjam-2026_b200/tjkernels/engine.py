@@ -120,6 +120,10 @@ class Engine:
         # Split-K workspace of the GEMMs, shared by all of them in order.
         self._gemm_ws: Optional[torch.Tensor] = None
         self._ln_ws: Optional[torch.Tensor] = None
+        # Workspaces that a larger row count has superseded: captured graphs
+        # of the smaller shapes still point at them, so they live until those
+        # graphs are released.
+        self._ln_ws_retired: List[torch.Tensor] = []
 
     # ---------------------------------------------------------------- weights
 
@@ -171,6 +175,7 @@ class Engine:
         self._gemm_ws = K.gemm_workspace(self.device)
         self._built_for = key
         self._graphs.clear()
+        self._ln_ws_retired.clear()
 
     def _build_tp(self, plan: Plan) -> None:
         """This rank's slice of every block (tensor-parallel layout); the
@@ -210,6 +215,7 @@ class Engine:
         self._gemm_ws = K.gemm_workspace(self.device)
         self._built_for = (plan.compute_dtype, self.dtype, self.device)
         self._graphs.clear()
+        self._ln_ws_retired.clear()
 
     # ---------------------------------------------------------------- compute
 
@@ -346,10 +352,14 @@ class Engine:
 
     def _ln_workspace(self, rows: int, d: int, device: torch.device) -> torch.Tensor:
         """The row-statistics workspace of tjb_gemm_add_layernorm, kept for the
-        largest row count seen (the kernels of one forward run in order)."""
+        largest row count seen (the kernels of one forward run in order).  A
+        workspace that a larger one replaces is kept alive, not freed: graphs
+        captured with it would otherwise replay into reused memory."""
         ws = self._ln_ws
         if ws is None or ws.device != device or ws.numel() < K.gemm_add_layernorm_workspace_bytes(
                 rows, d):
+            if ws is not None:
+                self._ln_ws_retired.append(ws)
             self._ln_ws = ws = K.gemm_add_layernorm_workspace(rows, d, device)
         return ws
 
