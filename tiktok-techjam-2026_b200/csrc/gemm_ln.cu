@@ -13,7 +13,8 @@
 // fp32: the residual chunk arrives by TMA in a 128-byte-swizzled staging
 // buffer (two per warp, the next chunk loading while this one is used), is
 // added to bias and accumulator, written back into the accumulator, and each
-// row's 128 values are reduced to (mean, M2).  The 2C partials of a row meet
+// row's 128 values are reduced to (mean, M2).  Each warp's 128 columns of
+// bias, gamma and beta are staged in shared memory once per tile.  The 2C partials of a row meet
 // in a global workspace: every warp publishes its 32 rows' partials and
 // counts in on its row block's counter; once all 8C warps of the block have,
 // each reads the 2C partials of its rows and combines them (Chan's formula
@@ -21,8 +22,8 @@
 // pass normalises and sends the residual and the LayerNorm output out of the
 // same staging buffers by TMA stores.  The GEMM's delta never reaches HBM and
 // the LayerNorm needs no pass of its own.  Waits on partners only ever point
-// to tiles of the same or a later round of the persistent loop, so with more
-// CTAs than C they cannot form a cycle; every wait is bounded.
+// to tiles of the same or a later round of the persistent loop, so with at
+// least C CTAs, all resident, they cannot form a cycle; every wait is bounded.
 #include "common.cuh"
 
 namespace tjb {
