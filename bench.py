@@ -23,7 +23,12 @@ and gathering the outputs back):
   e2e       the same call fed from pinned host memory: host->device copy of x
             and the mask, forward, device->host copy of the output, all timed.
   roofline  the dominant kernel (the tcgen05 GEMM) timed live with CUDA
-            events in an instrumented eager pass over the same input.
+            events in an instrumented eager pass over the same input, the
+            plan's kernel families unfused (``kernels``); ``kernels_plan``
+            times the plan's own kernels (the fused GEMM + LayerNorm among
+            them) the same way, and gives the launch count.
+  gpu_launches  library kernels launched in the timed steps (the plan's
+            launches per forward times the steps).
   cpu_baseline  the reference PyTorch CPU forward (the fp32 oracle
             restatement) on a bounded sample, rank 0 at N=1.
   clocks    SM clock median and throttle reasons sampled during the timed
