@@ -54,6 +54,34 @@ def test_argument_validation_without_device():
     assert lib.tjb_gemm_bias(fake, fake, None, fake, 1, 8, 8, 8, 8, 8, 0, 0, 0, None) == 4
 
 
+def test_gemm_add_layernorm_contract_without_device():
+    """The fused GEMM + LayerNorm sizes its workspace on the host and rejects
+    a missing or short workspace, unsupported widths and misaligned pointers
+    before any device work."""
+    from tjkernels import _lib
+    lib = _lib.lib()
+    for m, n in ((1, 256), (300, 1024), (16384, 768), (8192, 1024)):
+        blocks = -(-m // 128)
+        counters = -(-(2 * blocks * 4) // 256) * 256
+        assert lib.tjb_gemm_add_layernorm_workspace_bytes(m, n) == counters + (n // 256) * 2 * m * 8
+    assert lib.tjb_gemm_add_layernorm_workspace_bytes(0, 1024) == 256
+    fake = 1 << 20
+    f16, f32 = _lib.TJB_F16, _lib.TJB_F32
+
+    def call(n=1024, k=1024, ws=fake, ws_bytes=None, a=fake):
+        if ws_bytes is None:
+            ws_bytes = lib.tjb_gemm_add_layernorm_workspace_bytes(300, n)
+        return lib.tjb_gemm_add_layernorm(a, fake, fake, fake, fake, fake, fake, fake, 300, n,
+                                          k, 1e-5, f16, f32, None, None, ws, ws_bytes, None)
+
+    assert call(ws=None) == 1                                  # no workspace
+    assert call(ws_bytes=1024) == 1                            # workspace too small
+    assert call(n=2048) == 2                                   # wider than four 256-column tiles
+    assert call(n=1000) == 2                                   # not a multiple of 256
+    assert call(k=1020) == 2                                   # K not a multiple of 8
+    assert call(a=fake + 4) == 3                               # misaligned operand
+
+
 def test_kernel_error_carries_status():
     from tjkernels import _lib
     with pytest.raises(_lib.KernelError) as info:
