@@ -11,12 +11,15 @@ from oracle.model import ModelConfig, ReferenceModel, generate_case, oracle_forw
 def test_candidates_cover_the_knobs():
     from tjkernels import autotune, plans
     base = plans.Plan()
-    c512 = autotune.candidates(512, 2048, base)      # single-kernel FFN possible
-    c4096 = autotune.candidates(4096, 16384, base)   # not possible
-    assert len(c512) == 2 * len(c4096) == 32
+    c512 = autotune.candidates(512, 2048, base)      # single-kernel FFN, fused LN possible
+    c4096 = autotune.candidates(4096, 16384, base)   # neither
+    assert len(c512) == 6 * len(c4096) == 96
     assert {p.compute_dtype for p in c512} == {torch.float16, torch.bfloat16}
     assert all(p.delta_dtype in (torch.float32, p.compute_dtype) for p in c512)
     assert not any(p.ffn_single_kernel for p in c4096)
+    modes = {(p.fuse_layernorm, p.fuse_layernorm_ffn) for p in c512}
+    assert modes == {(False, True), (True, False), (True, True)}
+    assert not any(p.fuse_layernorm for p in c4096)
     assert len({tuple(sorted(p.to_json().items())) for p in c512}) == len(c512)
 
 

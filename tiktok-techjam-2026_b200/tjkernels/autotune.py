@@ -56,13 +56,18 @@ def candidates(d_model: int, ffn_dim: int, base: plans.Plan) -> List[plans.Plan]
     """The plan knobs worth sweeping on sm_100a."""
     out = []
     single = [False, True] if K.ffn_fused_supports(d_model, ffn_dim) else [False]
-    for cdt, delta32, dyn, split, one in itertools.product(
+    # LayerNorm placement: standalone, inside the out-projection only, or
+    # inside the out-projection and the FFN-out (widths the fused kernel takes).
+    ln_modes = [(False, True)]
+    if K.gemm_add_layernorm_supports(d_model):
+        ln_modes += [(True, False), (True, True)]
+    for cdt, delta32, dyn, split, one, (fuse, fuse_ffn) in itertools.product(
             (torch.float16, torch.bfloat16), (False, True), (True, False), (False, True),
-            single):
+            single, ln_modes):
         out.append(replace(base, compute_dtype=cdt,
                            delta_dtype=torch.float32 if delta32 else cdt,
                            attn_dynamic=dyn, gemm_stream_k=split, ffn_single_kernel=one,
-                           label="tuned"))
+                           fuse_layernorm=fuse, fuse_layernorm_ffn=fuse_ffn, label="tuned"))
     return out
 
 
