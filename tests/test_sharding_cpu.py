@@ -145,7 +145,9 @@ def _tp_worker(rank, world, port, out_q):
         x, mask = generate_case(cfg, 5, 0.5)
         with torch.no_grad():
             out = tp_torch_forward(enc, x, mask, rank, world)
-        out_q.put((rank, out))
+        # A numpy copy travels by value; a tensor would travel through shared
+        # memory that this process may remove by exiting before it is read.
+        out_q.put((rank, out.numpy().copy()))
     finally:
         dist.destroy_process_group()
 
@@ -165,11 +167,11 @@ def test_tensor_parallel_math_matches_unsharded(world):
         want = torch_forward(enc, x, mask)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29600 + world
+    port = _free_port()
     procs = [ctx.Process(target=_tp_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    outs = dict(q.get(timeout=180) for _ in range(world))
+    outs = {r: torch.from_numpy(a) for r, a in (q.get(timeout=180) for _ in range(world))}
     for p in procs:
         p.join(timeout=60)
     for r in range(world):
