@@ -1,7 +1,9 @@
 #!/usr/bin/env python3
 """Forward tokens/s of the sm_100a tjkernels engine (one process per GPU).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl tjb|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C]
+                    [--impl tjb|reference|reference-gpu]
+    python bench.py --kernel KIND DIMS... [options]     (one kernel, see below)
 
 Workload (``--config``, default 2): the BASELINE configs of the fused causal
 encoder forward.  Each GPU runs a full config-sized batch (weak scaling: the
@@ -22,18 +24,39 @@ steps with the inputs on GPU 0, each step scattering the shards over NVLink
 and gathering the outputs back):
   e2e       the same call fed from pinned host memory: host->device copy of x
             and the mask, forward, device->host copy of the output, all timed.
-  roofline  the dominant kernel (the tcgen05 GEMM) timed live with CUDA
-            events in an instrumented eager pass over the same input, the
-            plan's kernel families unfused (``kernels``); ``kernels_plan``
-            times the plan's own kernels (the fused GEMM + LayerNorm among
-            them) the same way, and gives the launch count.
+  roofline  the dominant kernel of the plan that was timed (the tcgen05 GEMM,
+            ``gemm_kernel``), each of its launches bracketed by CUDA events in
+            eager forwards of that same plan over the same input; divided by
+            the measured BURST peak (the launches are tens of microseconds
+            inside a short eager pass).  ``kernels_plan`` gives every kernel
+            family of the plan the same way, ``gemm_shapes`` the GEMM per
+            shape.
   gpu_launches  library kernels launched in the timed steps (the plan's
             launches per forward times the steps).
   cpu_baseline  the reference PyTorch CPU forward (the fp32 oracle
             restatement) on a bounded sample, rank 0 at N=1.
   clocks    SM clock median and throttle reasons sampled during the timed
             region (NVML).
-``--impl reference`` times the reference's CPU forward alone (rank 0 only).
+
+``--impl reference`` times the reference's CPU forward alone (rank 0 only),
+on a bounded sample of the workload (one sequence), and reports what it
+timed.  ``--impl reference-gpu`` runs the reference's own GPU path -- its
+``tjkernels`` engine (Triton attention and LayerNorm, cuBLAS GEMMs, its CUDA
+graph), unmodified, from ``baseline/_ref`` -- on the same workload through
+the harness's ``UserOptimizedTransformer``, and times its Triton attention
+(``flash_attention``) and add+LayerNorm (``fused_add_layernorm``) kernels at
+the config's shapes; ``--kernel attn|ln`` times this build's kernels at the
+same shapes the same way.
+
+``--kernel`` runs one library kernel on seeded fp16 inputs of a given shape,
+``--launches`` times with the L2 flushed before each, and prints the median
+CUDA-event time of all but the first launch (the command the single-kernel
+ncu captures are taken with):
+    --kernel gemm M N K [--act gelu] [--out f16|f32] [--stream-k]
+    --kernel attn B S H HD [--lengths full|prefix]
+    --kernel ln ROWS D
+    --kernel ffn T D F
+    --kernel gemm_ln M N K
 """
 
 from __future__ import annotations
@@ -52,7 +75,8 @@ from pathlib import Path
 import torch
 
 ROOT = Path(__file__).resolve().parent
-sys.path.insert(0, str(ROOT / "tiktok-techjam-2026_b200"))
+PKG_DIR = ROOT / "tiktok-techjam-2026_b200"
+REF_DIR = ROOT / "baseline" / "_ref"
 
 # cfg -> (batch, seq, d_model, heads, ffn, layers, padding_ratio); BASELINE.json configs.
 CONFIGS = {
@@ -71,6 +95,18 @@ CONFIG_NOTE = {
 }
 METRIC = "forward tokens/sec"
 FLUSH_BYTES = 256 << 20
+
+# DRAM traffic of the dominant kernel (gemm_kernel) per launch, averaged over
+# the launches of one forward of the config's tuned plan: sum of
+# dram__bytes_read.sum + dram__bytes_write.sum over those launches / their
+# number, from one ncu capture of this bench's own command (a one-pass
+# metric set on the full workload).  None where no capture was taken.
+GEMM_TRAFFIC_PER_LAUNCH = {}
+
+
+def use_package() -> None:
+    if str(PKG_DIR) not in sys.path:
+        sys.path.insert(0, str(PKG_DIR))
 
 
 def synthetic_case(b, s, d, seed, padding, rank=0, world=1):
@@ -95,16 +131,6 @@ def synthetic_case(b, s, d, seed, padding, rank=0, world=1):
     x = torch.stack(xs)
     mask = torch.arange(s)[None, :] < lengths[:, None]
     return x.masked_fill(~mask[..., None], 0), mask
-
-
-def layer_flops(b, s, d, h, f, lengths):
-    """Algorithmic FLOPs of one layer: GEMMs on the full padded shape,
-    causal attention on the valid lower triangle."""
-    t = b * s
-    hd = d // h
-    qkv, out, ffn = 6.0 * t * d * d, 2.0 * t * d * d, 4.0 * t * d * f
-    attn = sum(4.0 * h * hd * n * (n + 1) / 2 for n in lengths)
-    return qkv, out, ffn, attn
 
 
 def load_peaks():
@@ -181,7 +207,8 @@ class KernelTimer:
     def __init__(self, K, cfg):
         self.K = K
         self.cfg = cfg
-        self.records = []  # (name, start_event, end_event, flops, bytes, launches)
+        # (name, shape, start_event, end_event, flops, bytes, launches)
+        self.records = []
         self._orig = {}
 
     def _wrap(self, name, fn, cost):
@@ -191,8 +218,8 @@ class KernelTimer:
             s.record()
             out = fn(*args, **kwargs)
             e.record()
-            flops, nbytes, launches = cost(args, kwargs, out)
-            self.records.append((name, s, e, flops, nbytes, launches))
+            flops, nbytes, launches, shape = cost(args, kwargs, out)
+            self.records.append((name, shape, s, e, flops, nbytes, launches))
             return out
         return wrapped
 
@@ -207,11 +234,13 @@ class KernelTimer:
 
         def gemm_cost(args, kwargs, out):
             a, w = args[0], args[1]
-            return 2.0 * rows_of(a, kwargs) * a.shape[1] * w.shape[0], 0.0, 1
+            shape = f"M{a.shape[0]} N{w.shape[0]} K{a.shape[1]}"
+            return 2.0 * rows_of(a, kwargs) * a.shape[1] * w.shape[0], 0.0, 1, shape
 
         def ffn_cost(args, kwargs, out):
             h, w1 = args[0], args[1]
-            return 4.0 * rows_of(h, kwargs) * h.shape[1] * w1.shape[0], 0.0, 2
+            shape = f"T{h.shape[0]} d{h.shape[1]} F{w1.shape[0]}"
+            return 4.0 * rows_of(h, kwargs) * h.shape[1] * w1.shape[0], 0.0, 2, shape
 
         def ln_cost(args, kwargs, out):
             res, delta = args[0], args[1]
@@ -220,16 +249,17 @@ class KernelTimer:
             if delta is not None and kwargs.get("write_residual", True):
                 nbytes += n * 4
             nbytes += n * out[1].element_size()
-            return 0.0, float(nbytes), 1
+            return 0.0, float(nbytes), 1, f"rows{res.shape[0]} d{res.shape[1]}"
 
         def attn_cost(args, kwargs, out):
             qkv = args[0]
             b, s, _, h, hd = qkv.shape
             lengths = self.cfg["lengths"]
-            return sum(4.0 * h * hd * n * (n + 1) / 2 for n in lengths), 0.0, 1
+            flops = sum(4.0 * h * hd * n * (n + 1) / 2 for n in lengths)
+            return flops, 0.0, 1, f"B{b} S{s} H{h} hd{hd}"
 
         def mask_cost(args, kwargs, out):
-            return 0.0, 0.0, 1
+            return 0.0, 0.0, 1, ""
 
         for name, cost in (("gemm_bias", gemm_cost), ("fused_ffn", ffn_cost),
                            ("gemm_add_layernorm", gemm_cost),
@@ -243,21 +273,26 @@ class KernelTimer:
         for name, fn in self._orig.items():
             setattr(self.K, name, fn)
 
-    def summary(self, steps):
-        torch.cuda.synchronize()
+    @staticmethod
+    def _aggregate(records, key):
         agg = {}
-        for name, s, e, flops, nbytes, launches in self.records:
-            a = agg.setdefault(name, {"ms": 0.0, "flops": 0.0, "bytes": 0.0, "calls": 0,
-                                      "launches": 0})
+        for rec in records:
+            name, shape, s, e, flops, nbytes, launches = rec
+            a = agg.setdefault(key(rec), {"ms": 0.0, "flops": 0.0, "bytes": 0.0, "calls": 0,
+                                          "launches": 0})
             a["ms"] += s.elapsed_time(e)
             a["flops"] += flops
             a["bytes"] += nbytes
             a["calls"] += 1
             a["launches"] += launches
+        return agg
+
+    @staticmethod
+    def _rates(agg, steps):
         out = {}
-        for name, a in agg.items():
+        for k, a in agg.items():
             sec = a["ms"] / 1e3
-            out[name] = {
+            out[k] = {
                 "ms_per_step": a["ms"] / steps,
                 "calls_per_step": a["calls"] / steps,
                 "launches_per_step": a["launches"] / steps,
@@ -268,33 +303,29 @@ class KernelTimer:
             }
         return out
 
+    def summary(self, steps):
+        torch.cuda.synchronize()
+        return self._rates(self._aggregate(self.records, lambda r: r[0]), steps)
 
-def cpu_forward_rate(cfg_id, sample_batch, sample_layers, calls, seed=100000):
-    """Reference CPU forward (fp32 oracle restatement of BaselineTransformer)
-    on a bounded sample; returns (tokens/s for the full-depth forward, info)."""
-    from oracle.model import ModelConfig, build_model, generate_case
+    def gemm_shapes(self, steps):
+        """gemm_kernel launches (gemm_bias calls) per shape."""
+        recs = [r for r in self.records if r[0] == "gemm_bias"]
+        return self._rates(self._aggregate(recs, lambda r: r[1]), steps)
+
+
+# ---------------------------------------------------------------- CPU reference
+
+def cpu_reference_model(cfg_id, sample_batch, sample_layers):
+    """The reference CPU forward (fp32 oracle restatement of
+    BaselineTransformer) on a bounded sample of the config: ``sample_batch``
+    sequences and ``sample_layers`` of its layers.  Built once."""
+    from oracle.model import ModelConfig, build_model
 
     b, s, d, h, f, layers, pad = CONFIGS[cfg_id]
     torch.set_num_threads(os.cpu_count() or 1)
-    cfg = ModelConfig(sample_batch, s, d, h, f, sample_layers, True)
-    model = build_model(cfg, 0)
-    x, mask = generate_case(cfg, seed, pad)
     torch.set_float32_matmul_precision("highest")
-    times = []
-    with torch.inference_mode():
-        model(x, mask)  # warm-up
-        for _ in range(calls):
-            t0 = time.perf_counter_ns()
-            model(x, mask)
-            times.append((time.perf_counter_ns() - t0) / 1e9)
-    sec = statistics.median(times) * layers / sample_layers
-    tokens = sample_batch * s
-    info = {
-        "cores": torch.get_num_threads(),
-        "sample": f"{sample_batch} sequence(s) x S={s}, {sample_layers} of {layers} layers "
-                  f"(time scaled to {layers}), median of {calls} call(s) after 1 warm-up",
-    }
-    return tokens / sec, info
+    cfg = ModelConfig(sample_batch, s, d, h, f, sample_layers, True)
+    return cfg, build_model(cfg, 0)
 
 
 def cpu_sample_plan(cfg_id):
@@ -302,25 +333,64 @@ def cpu_sample_plan(cfg_id):
     return {0: (2, 4, 5), 1: (1, 4, 5), 2: (1, 4, 3), 3: (1, 1, 2), 4: (1, 1, 1)}[cfg_id]
 
 
+def cpu_forward_rate(cfg_id, calls, seed=100000):
+    """tokens/s of the full-depth forward, from the bounded sample's median
+    time scaled by layers / sample layers; returns (rate, info)."""
+    from oracle.model import generate_case
+
+    b, s, d, h, f, layers, pad = CONFIGS[cfg_id]
+    sb, sl, _ = cpu_sample_plan(cfg_id)
+    cfg, model = cpu_reference_model(cfg_id, sb, sl)
+    x, mask = generate_case(cfg, seed, pad)
+    times = []
+    with torch.inference_mode():
+        model(x, mask)  # warm-up
+        for _ in range(calls):
+            t0 = time.perf_counter_ns()
+            model(x, mask)
+            times.append((time.perf_counter_ns() - t0) / 1e9)
+    sec = statistics.median(times) * layers / sl
+    info = {
+        "cores": torch.get_num_threads(),
+        "sample": f"{sb} sequence(s) x S={s}, {sl} of {layers} layers "
+                  f"(time scaled to {layers}), median of {calls} call(s) after 1 warm-up",
+    }
+    return sb * s / sec, info
+
+
 def run_reference(args, rank, world):
+    """The reference arm: the reference's CPU forward on the host cores, rank
+    0 only.  Each step is one forward of the bounded sample (built once);
+    ``steps``/``ms_per_step`` describe exactly those timed forwards, and
+    ``value`` is their tokens/s scaled to the full depth."""
     if rank != 0:
         return
+    from oracle.model import generate_case
+
     b, s, d, h, f, layers, pad = CONFIGS[args.config]
     sb, sl, _ = cpu_sample_plan(args.config)
-    rates, info = [], None
-    for i in range(args.warmup + args.steps):
-        rate, info = cpu_forward_rate(args.config, sb, sl, 1, seed=100000 + i)
-        if i >= args.warmup:
-            rates.append(rate)
-    value = statistics.median(rates)
+    cfg, model = cpu_reference_model(args.config, sb, sl)
+    x, mask = generate_case(cfg, 100000, pad)
+    times = []
+    with torch.inference_mode():
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter_ns()
+            model(x, mask)
+            if i >= args.warmup:
+                times.append((time.perf_counter_ns() - t0) / 1e9)
+    ms_sample = statistics.median(times) * 1e3
+    value = sb * s / (ms_sample / 1e3 * layers / sl)
+    sample = (f"{sb} sequence(s) x S={s}, {sl} of {layers} layers per step "
+              f"(tokens/s scaled to {layers} layers), model built once")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": b * s / value * 1e3, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": ms_sample, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": workload_config(args.config, world),
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": info["cores"],
-                         "kind": "port", "sample": info["sample"]},
+        "config": dict(workload_config(args.config, world),
+                       timed_step=f"one CPU forward of the sample: {sample}"),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -342,13 +412,276 @@ def workload_config(cfg_id, world, tp=False):
             "l2": "flushed between timed steps (256 MiB write, untimed)"}
 
 
+# ---------------------------------------------------------------- shared timing
+
+def time_launches(fn, launches, flush=None):
+    """Median CUDA-event time (ms) of launches 2..n of ``fn`` (the first is a
+    warm-up); the L2 is flushed before each launch when ``flush`` is given."""
+    fn()
+    times = []
+    for _ in range(max(1, launches - 1)):
+        if flush is not None:
+            flush.zero_()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        fn()
+        end.record()
+        torch.cuda.synchronize()
+        times.append(start.elapsed_time(end))
+    return sorted(times)[len(times) // 2]
+
+
+def timed_steps(fwd, x, mask, steps, stream, flush):
+    """Mean device time (ms) of ``steps`` calls of fwd(x, mask), each
+    bracketed by CUDA events, L2 flushed between them (outside the events)."""
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        starts[i].record(stream)
+        fwd(x, mask)
+        ends[i].record(stream)
+        flush.zero_()
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(e) for a, e in zip(starts, ends)) / steps
+
+
+def e2e_leg(fwd, x_cpu, mask_cpu, steps, dev, stream, flush, barrier):
+    """Per-step ms of fwd fed from pinned host memory: every step copies its
+    input in and its output back, inside the timed region.  The copies run on
+    their own streams with two buffer sets, so step i+1's upload and step
+    i-1's download overlap step i's forward (what a serving loop does); the
+    L2 flush between forwards stays inside the timed region."""
+    x_host = x_cpu.pin_memory()
+    m_host = mask_cpu.pin_memory()
+    depth = 2
+    out_host = [torch.empty(x_cpu.shape, dtype=torch.float32).pin_memory()
+                for _ in range(depth)]
+    x_dev = [torch.empty(x_cpu.shape, dtype=x_cpu.dtype, device=dev) for _ in range(depth)]
+    m_dev = [torch.empty(mask_cpu.shape, dtype=mask_cpu.dtype, device=dev)
+             for _ in range(depth)]
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(depth)]
+    ev_comp = [torch.cuda.Event() for _ in range(depth)]
+
+    def run(n):
+        for i in range(n):
+            k = i % depth
+            with torch.cuda.stream(s_in):
+                if i >= depth:
+                    s_in.wait_event(ev_comp[k])  # forward i-2 is done with x_dev[k]
+                x_dev[k].copy_(x_host, non_blocking=True)
+                m_dev[k].copy_(m_host, non_blocking=True)
+                ev_in[k].record(s_in)
+            stream.wait_event(ev_in[k])
+            out = fwd(x_dev[k], m_dev[k])
+            ev_comp[k].record(stream)
+            flush.zero_()
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_comp[k])
+                out_host[k].copy_(out, non_blocking=True)
+                out.record_stream(s_out)
+
+    run(2 * depth)
+    torch.cuda.synchronize(dev)
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(dev)
+    e_start.record(s_in)
+    s_out.wait_event(e_start)
+    stream.wait_event(e_start)
+    run(steps)
+    e_end.record(s_out)
+    torch.cuda.synchronize(dev)
+    barrier()
+    return e_start.elapsed_time(e_end) / steps
+
+
+# -------------------------------------------------------- reference GPU path
+
+def run_reference_gpu(args, rank, world):
+    """The reference's own GPU implementation on this GPU, unmodified: the
+    harness's ``UserOptimizedTransformer`` whose forward is the reference's
+    ``tjkernels.forward`` (default plan on CUDA: fp16 compute, Triton causal
+    flash attention and add+LayerNorm, cuBLAS GEMMs, whole-forward graph when
+    the input is <= 64 MB), imported from ``baseline/_ref`` in a process
+    where this build's package is not on the path.  Rank 0 only."""
+    if rank != 0:
+        return
+    if not (REF_DIR / "tjkernels").is_dir() or not (REF_DIR / "torch_transformer_benchmark.py").exists():
+        print(json.dumps({"impl": "reference-gpu",
+                          "unavailable": "baseline/_ref holds no install of the reference"}),
+              flush=True)
+        return
+    sys.path[:] = [p for p in sys.path if Path(p or ".").resolve() != PKG_DIR]
+    sys.path.insert(0, str(REF_DIR))
+    import torch_transformer_benchmark as H  # the reference harness (imports its tjkernels)
+    import tjkernels as ref_tj
+    import tjkernels.kernels as ref_k
+    if Path(ref_tj.__file__).resolve().parent.parent != REF_DIR.resolve():
+        raise SystemExit(f"reference-gpu: imported tjkernels from {ref_tj.__file__}")
+
+    b, s, d, h, f, layers, pad = CONFIGS[args.config]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    # The harness's defaults (TF32 on for fp32 matmuls: --allow-tf32).
+    torch.backends.cuda.matmul.allow_tf32 = True
+    torch.backends.cudnn.allow_tf32 = True
+    torch.manual_seed(0)
+    model = H.UserOptimizedTransformer(H.TransformerConfig(b, s, d, h, f, layers, True))
+    model = model.to(dev).eval()
+    x_cpu, mask_cpu = synthetic_case(b, s, d, 100000, pad)
+    x, mask = x_cpu.to(dev), mask_cpu.to(dev)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            model(x, mask)
+        torch.cuda.synchronize()
+        plan = ref_tj.get_engine(model).plan
+        with ClockSampler(0) as clocks:
+            step_ms = timed_steps(model, x, mask, args.steps, stream, flush)
+        e2e_ms = e2e_leg(model, x_cpu, mask_cpu, args.steps, dev, stream, flush, lambda: None)
+
+        # The reference's two Triton kernels at this config's shapes, full
+        # lengths (its attention kernel has no length skipping), fp16.
+        g = torch.Generator(device=dev).manual_seed(0)
+        hd = d // h
+        qkv = torch.randn(b, s, 3, h, hd, device=dev, generator=g).half()
+        attn_ms = time_launches(lambda: ref_k.flash_attention(qkv, h, causal=True), 5, flush)
+        attn_flops = b * 4.0 * h * hd * s * (s + 1) / 2
+        res = torch.randn(b * s, d, device=dev, generator=g)
+        delta = torch.randn(b * s, d, device=dev, generator=g).half()
+        w, bvec = torch.ones(d, device=dev), torch.zeros(d, device=dev)
+        ln_ms = time_launches(lambda: ref_k.fused_add_layernorm(
+            res, delta, w, bvec, 1e-5, out_dtype=torch.float16), 5, flush)
+        ln_bytes = b * s * d * (4 + 2 + 4 + 2)
+    tokens = b * s
+    line = {
+        "impl": "reference-gpu", "metric": METRIC, "value": tokens / (step_ms / 1e3),
+        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": str(plan.compute_dtype).replace("torch.", ""),
+        "data": "synthetic (the same seeded inputs and default-init weights as this build's arm)",
+        "config": dict(workload_config(args.config, 1), plan=plan.to_json()),
+        "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": x_cpu.numel() * 4 + mask_cpu.numel(),
+                "d2h_bytes_per_step": tokens * d * 4, "ms_per_step": e2e_ms},
+        "kernels": {
+            "flash_attention": {"shape": f"B{b} S{s} H{h} hd{hd} causal full lengths fp16",
+                                "us": attn_ms * 1e3,
+                                "tflops": attn_flops / (attn_ms / 1e3) / 1e12},
+            "fused_add_layernorm": {"shape": f"rows{b * s} d{d} fp32 res, fp16 delta/out",
+                                    "us": ln_ms * 1e3,
+                                    "gbs": ln_bytes / (ln_ms / 1e3) / 1e9},
+            "timing": "median of 4 launches after 1 warm-up, L2 flushed before each",
+        },
+        "clocks": clocks.summary(),
+        "source": "reference tjkernels + harness, unmodified, from baseline/_ref",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------- single kernel
+
+def kernel_main(argv) -> int:
+    """One library kernel on seeded fp16 inputs (the profiling driver)."""
+    use_package()
+    import tjkernels.kernels as K
+
+    ap = argparse.ArgumentParser(prog="bench.py --kernel")
+    ap.add_argument("kernel", choices=["gemm", "attn", "ln", "ffn", "gemm_ln"])
+    ap.add_argument("dims", type=int, nargs="+")
+    ap.add_argument("--act", choices=["none", "gelu"], default="none")
+    ap.add_argument("--out", choices=["f16", "f32"], default="f16")
+    ap.add_argument("--lengths", choices=["full", "prefix"], default="full")
+    ap.add_argument("--stream-k", action="store_true", help="gemm: pass a stream-K workspace")
+    ap.add_argument("--launches", type=int, default=5)
+    args = ap.parse_args(argv)
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def randn(*shape, scale=1.0):
+        return (torch.randn(*shape, device=dev, generator=g) * scale).half()
+
+    nbytes = 0.0
+    if args.kernel == "gemm":
+        m, n, k = args.dims
+        a, w = randn(m, k), randn(n, k, scale=k ** -0.5)
+        bias = torch.randn(n, device=dev, generator=g)
+        out_dtype = torch.float16 if args.out == "f16" else torch.float32
+        act = K.ACT_GELU if args.act == "gelu" else K.ACT_NONE
+        ws = K.gemm_workspace(dev) if args.stream_k else None
+        fn = lambda: K.gemm_bias(a, w, bias, act=act, out_dtype=out_dtype, workspace=ws)
+        flops = 2.0 * m * n * k
+    elif args.kernel == "attn":
+        b, s, h, hd = args.dims
+        qkv = randn(b, s, 3, h, hd)
+        kw = {}
+        if args.lengths == "prefix":
+            lengths = torch.randint(s // 2, s + 1, (b,), device=dev, generator=g)
+            mask = torch.arange(s, device=dev)[None, :] < lengths[:, None]
+            lens, flags = K.mask_lengths(mask)
+            kw = dict(lengths=lens, key_mask=mask.to(torch.uint8), mask_flags=flags,
+                      sched=torch.zeros(2, dtype=torch.int32, device=dev))
+            n_list = lengths.tolist()
+        else:
+            n_list = [s] * b
+        fn = lambda: K.flash_attention(qkv, h, causal=True, **kw)
+        flops = sum(4.0 * h * hd * n * (n + 1) / 2 for n in n_list)
+    elif args.kernel == "ln":
+        rows, d = args.dims
+        res = torch.randn(rows, d, device=dev, generator=g)
+        delta = randn(rows, d)
+        w = torch.ones(d, device=dev)
+        bvec = torch.zeros(d, device=dev)
+        fn = lambda: K.fused_add_layernorm(res, delta, w, bvec, 1e-5, out_dtype=torch.float16,
+                                           residual_out=res)
+        flops, nbytes = 0.0, rows * d * (4.0 + 2 + 4 + 2)
+    elif args.kernel == "gemm_ln":
+        # GEMM + residual add + LayerNorm in one kernel, residual in place.
+        m, n, k = args.dims
+        a, w = randn(m, k), randn(n, k, scale=k ** -0.5)
+        bias = torch.randn(n, device=dev, generator=g)
+        res = torch.randn(m, n, device=dev, generator=g)
+        gamma = torch.ones(n, device=dev)
+        beta = torch.zeros(n, device=dev)
+        out = torch.empty(m, n, dtype=torch.float16, device=dev)
+        ws = K.gemm_add_layernorm_workspace(m, n, dev)
+        fn = lambda: K.gemm_add_layernorm(a, w, bias, res, gamma, beta, 1e-5,
+                                          residual_out=res, out=out, workspace=ws)
+        flops = 2.0 * m * n * k
+    else:
+        t, d, f = args.dims
+        h = randn(t, d)
+        w1, w2 = randn(f, d, scale=d ** -0.5), randn(d, f, scale=f ** -0.5)
+        b1 = torch.zeros(f, device=dev)
+        b2 = torch.zeros(d, device=dev)
+        fn = lambda: K.fused_ffn(h, w1, b1, w2, b2, out_dtype=torch.float16)
+        flops = 4.0 * t * d * f
+    ms = time_launches(fn, args.launches, flush)
+    rate = f"  {flops / ms / 1e9:.0f} TFLOP/s" if flops else ""
+    if nbytes:
+        rate += f"  {nbytes / ms / 1e6:.0f} GB/s"
+    print(f"{args.kernel} {args.dims}: {ms * 1e3:.1f} us{rate}", flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------- main
+
 def main():
+    if "--kernel" in sys.argv[1:]:
+        argv = list(sys.argv[1:])
+        argv.remove("--kernel")
+        sys.exit(kernel_main(argv))
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
-    ap.add_argument("--impl", default="tjb", choices=["tjb", "reference"])
+    ap.add_argument("--impl", default="tjb", choices=["tjb", "reference", "reference-gpu"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tp", action="store_true",
                     help="tensor-parallel over the N GPUs (strong scaling) instead of "
@@ -362,7 +695,11 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
+    if args.impl == "reference-gpu":
+        run_reference_gpu(args, rank, world)
+        return
 
+    use_package()
     import torch.distributed as dist
     import tjkernels
     import tjkernels.kernels as K
@@ -405,68 +742,14 @@ def main():
         plan = tjkernels.get_engine(model).plan
 
         # ----------------------------------------------------- timed region
-        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         barrier()
         torch.cuda.synchronize(dev)
         with ClockSampler(local) as clocks:
-            for i in range(args.steps):
-                starts[i].record(stream)
-                model(x, mask)
-                ends[i].record(stream)
-                flush.zero_()
-            torch.cuda.synchronize(dev)
+            step_ms = timed_steps(model, x, mask, args.steps, stream, flush)
         barrier()
-        step_ms = sum(a.elapsed_time(e) for a, e in zip(starts, ends)) / args.steps
 
         # ------------------------------------------------------- end to end
-        # Every step copies its input from pinned host memory and reads its
-        # output back, through the public call model(x, mask).  The copies run
-        # on their own streams with two buffer sets, so step i+1's upload and
-        # step i-1's download overlap step i's forward (what a serving loop
-        # does); the L2 flush between forwards stays inside the timed region.
-        x_host = x_cpu.pin_memory()
-        m_host = mask_cpu.pin_memory()
-        depth = 2
-        out_host = [torch.empty((b, s, d), dtype=torch.float32).pin_memory() for _ in range(depth)]
-        x_dev = [torch.empty_like(x) for _ in range(depth)]
-        m_dev = [torch.empty_like(mask) for _ in range(depth)]
-        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-        ev_in = [torch.cuda.Event() for _ in range(depth)]
-        ev_comp = [torch.cuda.Event() for _ in range(depth)]
-
-        def e2e_steps(n):
-            for i in range(n):
-                k = i % depth
-                with torch.cuda.stream(s_in):
-                    if i >= depth:
-                        s_in.wait_event(ev_comp[k])  # forward i-2 is done with x_dev[k]
-                    x_dev[k].copy_(x_host, non_blocking=True)
-                    m_dev[k].copy_(m_host, non_blocking=True)
-                    ev_in[k].record(s_in)
-                stream.wait_event(ev_in[k])
-                out = model(x_dev[k], m_dev[k])
-                ev_comp[k].record(stream)
-                flush.zero_()
-                with torch.cuda.stream(s_out):
-                    s_out.wait_event(ev_comp[k])
-                    out_host[k].copy_(out, non_blocking=True)
-                    out.record_stream(s_out)
-
-        e2e_steps(2 * depth)
-        torch.cuda.synchronize(dev)
-        e_start = torch.cuda.Event(enable_timing=True)
-        e_end = torch.cuda.Event(enable_timing=True)
-        barrier()
-        torch.cuda.synchronize(dev)
-        e_start.record(s_in)
-        s_out.wait_event(e_start)
-        stream.wait_event(e_start)
-        e2e_steps(args.steps)
-        e_end.record(s_out)
-        torch.cuda.synchronize(dev)
-        barrier()
-        e2e_ms = e_start.elapsed_time(e_end) / args.steps
+        e2e_ms = e2e_leg(model, x_cpu, mask_cpu, args.steps, dev, stream, flush, barrier)
 
         # ------------------------- scatter/gather from GPU 0 (N > 1 only)
         # The same steps with the inputs starting on GPU 0: each step
@@ -503,15 +786,12 @@ def main():
             sg_ms = sg_start.elapsed_time(sg_end) / args.steps
             del x_all, out_all
 
-        # -------------------------------------- per-kernel timing (eager)
+        # -------------------------------- per-kernel timing of the plan (eager)
+        # Eager forwards of the plan that was timed (graph off): each library
+        # call bracketed by CUDA events; gives the roofline's dominant kernel,
+        # the other families' rates and the launch count per forward.
         ksteps = max(3, min(args.steps, 20))
-        # Per-kernel rates come from the unfused form of the plan (each
-        # kernel family on its own: GEMMs, attention, FFN, LayerNorm); the
-        # launch count and the rates of the plan's own kernels (the fused
-        # GEMM + LayerNorm among them) from eager forwards of the plan itself.
-        plans.set_override(plans.Plan(compute_dtype=plan.compute_dtype,
-                                      delta_dtype=plan.delta_dtype, cuda_graph=False,
-                                      fuse_layernorm=False, label="instrumented"))
+        plans.set_override(dataclasses.replace(plan, cuda_graph=False))
         model(x, mask)
         torch.cuda.synchronize(dev)
         timer = KernelTimer(K, {"lengths": lengths, "valid_tokens": sum(lengths)})
@@ -519,38 +799,36 @@ def main():
             for _ in range(ksteps):
                 model(x, mask)
                 flush.zero_()
-        kern = timer.summary(ksteps)
-        plans.set_override(dataclasses.replace(plan, cuda_graph=False))
-        model(x, mask)
-        torch.cuda.synchronize(dev)
-        counter = KernelTimer(K, {"lengths": lengths, "valid_tokens": sum(lengths)})
-        with counter:
-            for _ in range(ksteps):
-                model(x, mask)
-                flush.zero_()
-        kern_plan = counter.summary(ksteps)
-        launches_real = sum(v["launches_per_step"] for v in kern_plan.values())
+        kern_plan = timer.summary(ksteps)
+        gemm_shapes = timer.gemm_shapes(ksteps)
+        launches_per_step = sum(v["launches_per_step"] for v in kern_plan.values())
         plans.set_override(None)
 
     status_local = float(K.device_status(clear=True))  # synchronises; after all timing
     step_max, e2e_max, sg_max, status_max = max_over_ranks([step_ms, e2e_ms, sg_ms,
                                                             status_local])
     device_status = int(status_max)
-    launches_per_step = launches_real
 
     if rank == 0:
         peaks = load_peaks()
         tokens = b * s * (1 if tp else world)
         value = tokens / (step_max / 1e3)
-        gemm_ms = (kern["gemm_bias"]["ms_per_step"] + kern["fused_ffn"]["ms_per_step"])
-        gemm_flops = (kern["gemm_bias"]["flops_per_call"] * kern["gemm_bias"]["calls_per_step"]
-                      + kern["fused_ffn"]["flops_per_call"] * kern["fused_ffn"]["calls_per_step"])
-        gemm_launches = (kern["gemm_bias"]["launches_per_step"]
-                         + kern["fused_ffn"]["launches_per_step"])
+        # The dominant kernel: gemm_kernel, launched by gemm_bias (one launch
+        # per call) and fused_ffn (two per call).
+        fams = [kern_plan[n] for n in ("gemm_bias", "fused_ffn") if n in kern_plan]
+        gemm_ms = sum(v["ms_per_step"] for v in fams)
+        gemm_flops = sum(v["flops_per_call"] * v["calls_per_step"] for v in fams)
+        gemm_launches = sum(v["launches_per_step"] for v in fams)
         achieved = gemm_flops / (gemm_ms / 1e3) / 1e12
-        peak = peaks["tflops_sustained"]
-        attn = kern["flash_attention"]
-        ln = kern["fused_add_layernorm"]
+        peak = peaks["tflops"]
+        traffic = GEMM_TRAFFIC_PER_LAUNCH.get(args.config) if not tp else None
+
+        def rate(name, key="tflops"):
+            return kern_plan.get(name, {}).get(key)
+
+        def frac(v, p):
+            return None if v is None else v / p
+
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_max,
@@ -561,24 +839,29 @@ def main():
             "config": dict(workload_config(args.config, world, tp),
                            plan=plan.to_json()),
             "roofline": {
-                "bound": "tensor", "kernel": "gemm_kernel (tcgen05, all GEMM launches)",
+                "bound": "tensor",
+                "kernel": "gemm_kernel (tcgen05; every launch of it in the timed plan)",
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak,
-                "peak_note": f"{peaks['source']} sustained bf16/f16 dense "
-                             f"(burst {peaks['tflops']})",
+                "peak_note": f"{peaks['source']} burst bf16/f16 dense (sustained "
+                             f"{peaks['tflops_sustained']}); FLOPs on valid tokens",
                 "flops_per_launch": gemm_flops / gemm_launches,
                 "ms_per_launch": gemm_ms / gemm_launches,
-                "traffic": None,
-                "attn_tflops": attn["tflops"], "attn_frac": attn["tflops"] / peak,
-                "ffn_tflops": kern["fused_ffn"]["tflops"],
-                "ffn_frac": kern["fused_ffn"]["tflops"] / peak,
-                # The plan's fused GEMM + add + LayerNorm (when it runs one).
-                "gemm_ln_tflops": kern_plan.get("gemm_add_layernorm", {}).get("tflops"),
-                "layernorm_gbs": ln["gbs"], "layernorm_frac": ln["gbs"] / peaks["hbm_gbs"],
-                "eager_step_ms": sum(v["ms_per_step"] for v in kern.values()),
+                "traffic": traffic,
+                "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum per launch of "
+                                "gemm_kernel, mean over one forward's launches, one ncu "
+                                "capture of this command" if traffic else None,
+                "attn_tflops": rate("flash_attention"),
+                "attn_frac": frac(rate("flash_attention"), peak),
+                "ffn_tflops": rate("fused_ffn"), "ffn_frac": frac(rate("fused_ffn"), peak),
+                "gemm_ln_tflops": rate("gemm_add_layernorm"),
+                "gemm_ln_frac": frac(rate("gemm_add_layernorm"), peak),
+                "layernorm_gbs": rate("fused_add_layernorm", "gbs"),
+                "layernorm_frac": frac(rate("fused_add_layernorm", "gbs"), peaks["hbm_gbs"]),
+                "eager_step_ms": sum(v["ms_per_step"] for v in kern_plan.values()),
             },
-            "kernels": kern,
             "kernels_plan": kern_plan,
+            "gemm_shapes": gemm_shapes,
             "e2e": {"value": tokens / (e2e_max / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": x_cpu.numel() * 4 + mask_cpu.numel(),
                     "d2h_bytes_per_step": b * s * d * 4, "ms_per_step": e2e_max,
@@ -601,10 +884,10 @@ def main():
             raise SystemExit(f"a kernel recorded device status {device_status} "
                              "(bounded wait ran out): run invalid")
         if world == 1 and not args.no_cpu_baseline:
-            sb, sl, calls = cpu_sample_plan(args.config)
-            rate, info = cpu_forward_rate(args.config, sb, sl, calls)
-            line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": info["cores"],
-                                    "kind": "port", "sample": info["sample"]}
+            rate_cpu, info = cpu_forward_rate(args.config, cpu_sample_plan(args.config)[2])
+            line["cpu_baseline"] = {"value": rate_cpu, "unit": "tokens/s",
+                                    "cores": info["cores"], "kind": "port",
+                                    "sample": info["sample"]}
         print(json.dumps(line), flush=True)
 
     if world > 1:

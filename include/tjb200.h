@@ -97,8 +97,10 @@ int tjb_add_layernorm_tiles(const float* res, const void* delta, float* res_out,
  * written); out: f32/f16/bf16 contiguous.  N = 256, 512, 768 or 1024, K % 8
  * == 0.  The N/256 tiles of a 128-row block exchange per-row (mean, M2)
  * partials through `workspace` (tjb_gemm_add_layernorm_workspace_bytes(M, N)
- * bytes, 16-byte aligned, zero before the first call; every call leaves its
- * counters zero again; calls that may overlap need separate workspaces).
+ * bytes, 16-byte aligned, zero before the first call; every call that
+ * completes leaves its counters zero again, but one whose bounded wait ran
+ * out (TJB_ERR_DEVICE_TIMEOUT) may not: zero the workspace again before the
+ * next call; calls that may overlap need separate workspaces).
  * row_mask (nullable): rows with 0 get a zero output row; m_tiles (nullable)
  * as in tjb_row_tiles.  Replaces the out-projection / FFN-out torch.addmm and
  * the fused_add_layernorm that follows it (tjkernels/engine.py:247-256;
@@ -250,7 +252,10 @@ int tjb_ffn_fused(const void* h, const void* w1, const float* b1, const void* w2
  * (a fixed memory pool with no allocator hook, or a path where an allocation
  * may not block or fail).  Every GPU that loads the library holds the array
  * until exit.  The first call on a device looks up the array's device
- * address; make it before any stream capture.  All calls share the array:
+ * address (and, with lazy module loading, loads the library's device code
+ * there, which can take device memory): make it at set-up time, before any
+ * stream capture.  The address is cached for the process and does not
+ * survive cudaDeviceReset.  All calls share the array:
  * calls that overlap on the GPU race and must be serialised by the caller.
  * No counterpart in the reference.
  */
@@ -299,6 +304,22 @@ const char* tjb_last_cuda_error(void);
  * waits).
  */
 int tjb_device_status(int clear);
+
+/*
+ * Stream-ordered snapshot of the device status word: copies it into
+ * *host_dst (pinned host memory, 4-byte aligned) once every kernel enqueued
+ * on `stream` before this call has finished.  Does not synchronise and
+ * launches no kernel, so it may sit at the end of a captured CUDA graph; the
+ * caller reads *host_dst later (after its next synchronisation, or at its
+ * next call) and treats a non-zero value as TJB_ERR_DEVICE_TIMEOUT.
+ * After a timeout the library's scratch state may be left mid-update:
+ * every caller-owned workspace (tjb_gemm_add_layernorm's counters, the
+ * stream-K workspace, the attention work counter) must be zero-filled again
+ * before its next use, and the status cleared with tjb_device_status(1).
+ * No counterpart in the reference (its Triton kernels have no device-side
+ * waits).
+ */
+int tjb_device_status_async(int32_t* host_dst, tjb_stream_t stream);
 
 /*
  * Self-test of the bounded device-side wait: one thread spins on *flag

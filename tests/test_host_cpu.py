@@ -82,6 +82,26 @@ def test_gemm_add_layernorm_contract_without_device():
     assert call(a=fake + 4) == 3                               # misaligned operand
 
 
+def test_ffn_noalloc_limit_without_device():
+    """The allocation-free FFN refuses T * F beyond its fixed array before it
+    touches a device or a pointer (so the pointers here are never used)."""
+    from tjkernels import _lib
+    lib = _lib.lib()
+    fake = 1 << 20
+    too_many_rows = (8 << 20) // 64 + 1
+    assert lib.tjb_ffn_noalloc(fake, fake, fake, fake, fake, fake, too_many_rows, 64, 64,
+                               _lib.TJB_F16, _lib.TJB_F32, None) == 2
+    assert lib.tjb_ffn_noalloc(None, fake, fake, fake, fake, fake, 8, 64, 64,
+                               _lib.TJB_F16, _lib.TJB_F32, None) == 1
+
+
+def test_device_status_async_validation_without_device():
+    from tjkernels import _lib
+    lib = _lib.lib()
+    assert lib.tjb_device_status_async(None, None) == 1
+    assert lib.tjb_device_status_async((1 << 20) + 2, None) == 1  # not 4-byte aligned
+
+
 def test_kernel_error_carries_status():
     from tjkernels import _lib
     with pytest.raises(_lib.KernelError) as info:

@@ -2,10 +2,18 @@
 unsharded torch forward within the per-element budget.  Skipped with fewer
 than two GPUs."""
 
+import socket
+
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
 
 
 def _worker(rank, world, port, out_q):
@@ -43,12 +51,21 @@ def test_tensor_parallel_two_gpus():
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, 29710, q)) for r in range(2)]
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    results = [q.get(timeout=300) for _ in range(2)]
-    for p in procs:
-        p.join(timeout=60)
+    try:
+        results = [q.get(timeout=300) for _ in range(2)]
+    finally:
+        # A worker that failed, or is still waiting on its peer, must not keep
+        # holding its GPU after the test.
+        for p in procs:
+            p.join(timeout=60)
+        for p in procs:
+            if p.is_alive():
+                p.terminate()
+                p.join(timeout=30)
     for rank, usage, zero in results:
         print(f"tensor parallel rank {rank}: budget usage {usage:.3f}")
         assert usage <= 1.0, (rank, usage)

@@ -3,10 +3,11 @@
 tjb_ffn_noalloc exists for callers that cannot allocate device memory when
 they call in (a fixed memory pool with no allocator hook, or a path where an
 allocation may not block or fail): it keeps the FFN's hidden activations in a
-fixed 16 MiB array inside the library instead of caller scratch.  Its output
-must match tjb_ffn's, which takes the scratch from the caller, and it must
-keep matching on a second call, when the shared array still holds the first
-call's contents.  This file is collected last on purpose.
+fixed 16 MiB array inside the library instead of caller scratch.  It runs the
+same two GEMMs on the same inputs as tjb_ffn, which takes that scratch from
+the caller, so its output must be bit-identical -- on the first call and on a
+second call, when the shared array still holds the first call's contents.
+This file is collected last on purpose.
 """
 
 import math
@@ -45,19 +46,22 @@ def test_noalloc_matches_ffn_twice():
                                        w2.data_ptr(), b2.data_ptr(), got.data_ptr(), t, d, f,
                                        _lib.TJB_F16, _lib.TJB_F32, stream), "tjb_ffn_noalloc")
         torch.cuda.synchronize()
-        assert torch.isfinite(got).all()
-        # Same GEMMs on the same inputs; the tolerance of the FFN kernel test.
-        assert (got - ref).abs().max().item() < 2e-2
+        # Same kernels, same operands, same order of summation: bit-identical.
+        assert torch.equal(got, ref)
 
 
 def test_noalloc_rejects_oversize():
+    """T * F one past the array's limit is refused before anything launches.
+    Every buffer is as large as the shape claims, so even a regressed guard
+    could not read or write outside them."""
     from tjkernels import _lib
     lib = _lib.lib()
-    h, w1, b1, w2, b2 = _ffn_pair(8, 64, 64, 3)
-    out = torch.zeros(8, 64, device="cuda")
-    too_many_rows = (8 << 20) // 64 + 1  # T * F just over the 8 Mi-element limit
+    d, f = 64, 64
+    t = (8 << 20) // f + 1  # T * F just over the 8 Mi-element limit
+    h, w1, b1, w2, b2 = _ffn_pair(t, d, f, 3)
+    out = torch.zeros(t, d, device="cuda")
     status = lib.tjb_ffn_noalloc(h.data_ptr(), w1.data_ptr(), b1.data_ptr(), w2.data_ptr(),
-                                 b2.data_ptr(), out.data_ptr(), too_many_rows, 64, 64,
+                                 b2.data_ptr(), out.data_ptr(), t, d, f,
                                  _lib.TJB_F16, _lib.TJB_F32,
                                  torch.cuda.current_stream().cuda_stream)
     assert status == 2  # TJB_ERR_BAD_SHAPE, nothing launched

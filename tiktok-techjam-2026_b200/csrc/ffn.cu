@@ -55,7 +55,12 @@ extern "C" int tjb_ffn(const void* h, const void* w1, const float* b1, const voi
 // In host code the array's name is only a host-side stand-in, never a device
 // address, so its device address is looked up once per device with
 // cudaGetSymbolAddress (with that device current) and cached.  The first
-// call on a device does that look-up; make it before any stream capture.
+// call on a device does that look-up, and with CUDA's lazy module loading it
+// is also where the library's device code (the array included) gets loaded
+// onto that device, which may itself take device memory: make the first call
+// at set-up time, before any stream capture.  The cached address belongs to
+// the device's current primary context; it does not survive a
+// cudaDeviceReset, after which the library must be reloaded (a new process).
 // All calls share the one array: the hidden tile is fully written by the
 // first GEMM before the second reads it, so nothing needs clearing between
 // calls, but calls that overlap on the GPU (different streams, or two

@@ -262,6 +262,18 @@ int tjb_device_status(int clear) {
   return v;
 }
 
+int tjb_device_status_async(int32_t* host_dst, tjb_stream_t stream) {
+  if (!host_dst || (reinterpret_cast<uintptr_t>(host_dst) & 3u) != 0)
+    return TJB_ERR_INVALID_ARGUMENT;
+  if (!tjb::device_ok()) return TJB_ERR_NO_DEVICE;
+  // A copy-engine read of the word, ordered after every kernel already on
+  // the stream; nothing is launched and nothing waits on the host.
+  return tjb::cuda_status(cudaMemcpyFromSymbolAsync(host_dst, tjb::g_device_status,
+                                                    sizeof(int32_t), 0,
+                                                    cudaMemcpyDeviceToHost,
+                                                    reinterpret_cast<cudaStream_t>(stream)));
+}
+
 int tjb_mask_lengths(const uint8_t* mask, int B, int S, int32_t* lengths, int32_t* flags,
                      tjb_stream_t stream) {
   if (!mask || !lengths || !flags || B <= 0 || S <= 0) return TJB_ERR_INVALID_ARGUMENT;

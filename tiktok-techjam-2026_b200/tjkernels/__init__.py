@@ -1,16 +1,14 @@
-"""tjkernels (B200 build) -- the fused causal Transformer-encoder forward on
-hand-written sm_100a CUDA kernels, as a drop-in for the TechJam 2026
-``tjkernels`` package.
+"""B200 (sm_100a) engine for the causal pre-LN encoder forward.
 
-Public entry point, unchanged from the reference::
-
-    import tjkernels
-    class UserOptimizedTransformer(BaselineTransformer):
-        def forward(self, x, valid_token_mask=None):
-            return tjkernels.forward(self, x, valid_token_mask)
-
-The engine reads parameters directly off the baseline module, so the
-harness's strict ``load_state_dict`` weight copy keeps working unchanged.
+A benchmark module opts in by routing its ``forward`` to ``forward(self, x,
+valid_token_mask)``; everything else -- packing the module's weights into
+fp16 tensor-core layouts, choosing a per-shape ``Plan``, running the CUDA
+kernels of ``libtjb200.so`` and replaying the whole forward as a CUDA graph
+-- happens behind that one call.  The module keeps owning its parameters
+(the engine only reads them), so copying weights into it with
+``load_state_dict`` needs nothing special.  ``get_engine`` returns the
+engine cached on a module, ``reset_engines`` drops it, and ``select_plan``
+shows which plan a shape gets.
 """
 
 from .engine import forward, get_engine, reset_engines

@@ -11,11 +11,8 @@ import ctypes
 import threading
 from pathlib import Path
 
-import os
-
-# The in-tree build; TJB_LIBRARY may name another build of the same ABI.
-LIB_PATH = Path(os.environ.get("TJB_LIBRARY") or
-                Path(__file__).resolve().with_name("libtjb200.so"))
+# The in-tree build (tiktok-techjam-2026_b200/build.py writes it here).
+LIB_PATH = Path(__file__).resolve().with_name("libtjb200.so")
 
 TJB_F32, TJB_F16, TJB_BF16 = 0, 1, 2
 
@@ -59,6 +56,7 @@ SIGNATURES = {
                                  _c_int, _p]),
     "tjb_mask_lengths": (_c_int, [_p, _c_int, _c_int, _p, _p, _p]),
     "tjb_device_status": (_c_int, [_c_int]),
+    "tjb_device_status_async": (_c_int, [_p, _p]),
     "tjb_selftest_wait": (_c_int, [_p, _c_i64, _p]),
 }
 

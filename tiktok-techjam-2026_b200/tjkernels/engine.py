@@ -124,6 +124,12 @@ class Engine:
         # of the smaller shapes still point at them, so they live until those
         # graphs are released.
         self._ln_ws_retired: List[torch.Tensor] = []
+        # Pinned host word that every forward ends by copying the device
+        # status word into (stream-ordered, no host synchronisation; part of
+        # the captured graph too).  The next call reads it: non-zero means a
+        # kernel's bounded wait ran out, which can leave the workspaces above
+        # mid-update, so they are zeroed again and the call raises.
+        self._status_host: Optional[torch.Tensor] = None
 
     # ---------------------------------------------------------------- weights
 
@@ -173,6 +179,7 @@ class Engine:
         self.layers = layers
         self._attn_sched = torch.zeros(2, dtype=torch.int32, device=self.device)
         self._gemm_ws = K.gemm_workspace(self.device)
+        self._status_host = torch.zeros(1, dtype=torch.int32).pin_memory()
         self._built_for = key
         self._graphs.clear()
         self._ln_ws_retired.clear()
@@ -213,6 +220,7 @@ class Engine:
         self.layers = layers
         self._attn_sched = torch.zeros(2, dtype=torch.int32, device=self.device)
         self._gemm_ws = K.gemm_workspace(self.device)
+        self._status_host = torch.zeros(1, dtype=torch.int32).pin_memory()
         self._built_for = (plan.compute_dtype, self.dtype, self.device)
         self._graphs.clear()
         self._ln_ws_retired.clear()
@@ -363,11 +371,51 @@ class Engine:
             self._ln_ws = ws = K.gemm_add_layernorm_workspace(rows, d, device)
         return ws
 
+    def _forward_reported(self, x: torch.Tensor, mask: Optional[torch.Tensor]) -> torch.Tensor:
+        """The forward followed by the stream-ordered status snapshot."""
+        out = self._forward_impl(x, mask)
+        K.device_status_async(self._status_host, self.device)
+        return out
+
+    # ----------------------------------------------------------------- status
+
+    def check_status(self, synchronize: bool = True) -> None:
+        """Raise ``KernelError`` (TJB_ERR_DEVICE_TIMEOUT) if a kernel of an
+        earlier forward recorded that one of its bounded device-side waits
+        ran out.  Every call does this check without synchronising (it sees
+        the forwards that have finished by then); ``synchronize=True`` waits
+        for all of them first."""
+        if self._status_host is None:
+            return
+        if synchronize:
+            torch.cuda.synchronize(self.device)
+        if int(self._status_host[0]) != 0:
+            self._recover()
+
+    def _recover(self) -> None:
+        """After a device-side timeout: clear the device status word, zero
+        every workspace a kernel may have left mid-update (row-statistics
+        counters, stream-K counters, the attention work counter) and raise."""
+        from ._lib import KernelError
+
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize(self.device)
+            status = K.device_status(clear=True) or int(self._status_host[0])
+            for ws in (self._gemm_ws, self._ln_ws, self._attn_sched, *self._ln_ws_retired):
+                if ws is not None:
+                    ws.zero_()
+            torch.cuda.synchronize(self.device)
+        self._status_host.zero_()
+        raise KernelError("tjkernels forward", status,
+                          "a device-side wait of an earlier forward ran out (its output is "
+                          "not valid); workspaces re-zeroed, the next call runs normally")
+
     # ------------------------------------------------------------------- call
 
     def __call__(self, x: torch.Tensor, mask: Optional[torch.Tensor] = None) -> torch.Tensor:
         if not x.is_cuda:
             raise RuntimeError("tjkernels runs on CUDA (sm_100) tensors only; no CPU fallback")
+        self.check_status(synchronize=False)
         batch, seq, _ = x.shape
         plan = None if plans.has_override() else self._plan_cache.get((batch, seq))
         if plan is None:
@@ -379,8 +427,8 @@ class Engine:
         self._build(plan)
         if plan.cuda_graph and self._tp is None:
             key = (tuple(x.shape), x.dtype, mask is not None, plan)
-            return self._graphs.get(key, self._forward_impl, x, mask).run(x, mask)
-        return self._forward_impl(x, mask)
+            return self._graphs.get(key, self._forward_reported, x, mask).run(x, mask)
+        return self._forward_reported(x, mask)
 
 
 def get_engine(module: torch.nn.Module) -> Engine:

@@ -322,6 +322,17 @@ def device_status(clear: bool = False) -> int:
     return int(_lib.lib().tjb_device_status(int(clear)))
 
 
+def device_status_async(dst: torch.Tensor, device: torch.device) -> None:
+    """Enqueue, on the current stream of ``device``, a copy of the device
+    status word into ``dst`` (a pinned host int32 tensor) that lands once the
+    kernels queued before it have finished; no synchronisation, so it may be
+    captured at the end of a CUDA graph."""
+    if dst.is_cuda or dst.dtype != torch.int32 or not dst.is_pinned():
+        raise TypeError("device_status_async writes into a pinned host int32 tensor")
+    status = _lib.lib().tjb_device_status_async(_ptr(dst), _stream(device))
+    _lib.check(status, "tjb_device_status_async")
+
+
 __all__ = [
     "ACT_NONE", "ACT_GELU", "fused_add_layernorm", "layernorm", "gemm_bias", "gemm_workspace",
     "gemm_add_layernorm_workspace", "gemm_add_layernorm_workspace_bytes",
@@ -329,4 +340,5 @@ __all__ = [
     "fused_ffn",
     "ffn_single_kernel", "ffn_fused_supports",
     "flash_attention", "flash_supports", "mask_lengths", "row_tiles", "device_status",
+    "device_status_async",
 ]
