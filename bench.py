@@ -55,7 +55,8 @@ ncu captures are taken with):
     --kernel gemm M N K [--act gelu] [--out f16|f32] [--stream-k]
     --kernel attn B S H HD [--lengths full|prefix]
     --kernel ln ROWS D
-    --kernel ffn T D F
+    --kernel ffn T D F            (two launches)
+    --kernel ffn_single T D F     (one kernel, hidden on chip; d <= 1024)
     --kernel gemm_ln M N K
 """
 
@@ -101,7 +102,10 @@ FLUSH_BYTES = 256 << 20
 # dram__bytes_read.sum + dram__bytes_write.sum over those launches / their
 # number, from one ncu capture of this bench's own command (a one-pass
 # metric set on the full workload).  None where no capture was taken.
-GEMM_TRAFFIC_PER_LAUNCH = {}
+# Config 2: 12 launches (QKV 17.7-18.5 MB, FFN1 20.1-20.4 MB, FFN2 64.4-66.4
+# MB each); the outputs mostly stay in the 126 MB L2 during a launch, so the
+# figure sits below the algorithmic bytes (A + W read, C written).
+GEMM_TRAFFIC_PER_LAUNCH = {2: 34.44e6}
 
 
 def use_package() -> None:
@@ -591,7 +595,7 @@ def kernel_main(argv) -> int:
     import tjkernels.kernels as K
 
     ap = argparse.ArgumentParser(prog="bench.py --kernel")
-    ap.add_argument("kernel", choices=["gemm", "attn", "ln", "ffn", "gemm_ln"])
+    ap.add_argument("kernel", choices=["gemm", "attn", "ln", "ffn", "ffn_single", "gemm_ln"])
     ap.add_argument("dims", type=int, nargs="+")
     ap.add_argument("--act", choices=["none", "gelu"], default="none")
     ap.add_argument("--out", choices=["f16", "f32"], default="f16")
@@ -654,12 +658,17 @@ def kernel_main(argv) -> int:
                                           residual_out=res, out=out, workspace=ws)
         flops = 2.0 * m * n * k
     else:
+        # ffn: the two GEMM launches through a hidden scratch; ffn_single: the
+        # one-kernel form whose hidden activations stay on chip.
         t, d, f = args.dims
         h = randn(t, d)
         w1, w2 = randn(f, d, scale=d ** -0.5), randn(d, f, scale=f ** -0.5)
         b1 = torch.zeros(f, device=dev)
         b2 = torch.zeros(d, device=dev)
-        fn = lambda: K.fused_ffn(h, w1, b1, w2, b2, out_dtype=torch.float16)
+        if args.kernel == "ffn":
+            fn = lambda: K.fused_ffn(h, w1, b1, w2, b2, out_dtype=torch.float16)
+        else:
+            fn = lambda: K.ffn_single_kernel(h, w1, b1, w2, b2, out_dtype=torch.float16)
         flops = 4.0 * t * d * f
     ms = time_launches(fn, args.launches, flush)
     rate = f"  {flops / ms / 1e9:.0f} TFLOP/s" if flops else ""
@@ -714,7 +723,10 @@ def main():
     b, s, d, h, f, layers, pad = CONFIGS[args.config]
     cfg = EncoderConfig(b, s, d, h, f, layers, True)
     torch.manual_seed(0)
-    model = Encoder(cfg).to(dev).eval()
+    # Default initialisation, drawn on the GPU itself (config 4's 2.4 B
+    # parameters take tens of seconds to initialise on the host).
+    with torch.device(dev):
+        model = Encoder(cfg).eval()
     tp = args.tp and world > 1
     if tp:
         from tjkernels.parallel import enable_tensor_parallel
@@ -752,34 +764,57 @@ def main():
         e2e_ms = e2e_leg(model, x_cpu, mask_cpu, args.steps, dev, stream, flush, barrier)
 
         # ------------------------- scatter/gather from GPU 0 (N > 1 only)
-        # The same steps with the inputs starting on GPU 0: each step
-        # scatters the ranks' shards over NVLink (NCCL), runs the forward on
-        # every GPU and gathers the outputs back to GPU 0.
+        # The same steps with the inputs starting on GPU 0: each step's
+        # shards are scattered from GPU 0 over NVLink (NCCL), every GPU runs
+        # its forward, and the outputs are gathered back to GPU 0.  As in a
+        # serving loop, the collectives run on their own stream with two
+        # buffer sets: step i+1's scatter and step i's gather overlap the
+        # forwards (every rank issues them in the same order).
         sg_ms = 0.0
         if world > 1 and not tp:
+            depth = 2
             x_all = None
-            out_all = None
+            out_all = [None] * depth
             if rank == 0:
                 x_all = [synthetic_case(b, s, d, 100000, pad, r, world)[0].to(dev)
                          for r in range(world)]
-                out_all = [torch.empty((b, s, d), dtype=torch.float32, device=dev)
-                           for _ in range(world)]
-            x_sg = torch.empty_like(x)
+                out_all = [[torch.empty((b, s, d), dtype=torch.float32, device=dev)
+                            for _ in range(world)] for _ in range(depth)]
+            x_sg = [torch.empty_like(x) for _ in range(depth)]
+            comm = torch.cuda.Stream(dev)
+            ev_in = [torch.cuda.Event() for _ in range(depth)]
+            ev_done = [torch.cuda.Event() for _ in range(depth)]
 
-            def sg_step():
-                dist.scatter(x_sg, x_all, src=0)
-                dist.gather(model(x_sg, mask), out_all, dst=0)
+            def sg_steps(n):
+                with torch.cuda.stream(comm):
+                    comm.wait_stream(stream)
+                    dist.scatter(x_sg[0], x_all, src=0)
+                    ev_in[0].record(comm)
+                for i in range(n):
+                    k, kn = i % depth, (i + 1) % depth
+                    if i + 1 < n:
+                        with torch.cuda.stream(comm):
+                            if i >= 1:
+                                comm.wait_event(ev_done[kn])  # forward i-1 read x_sg[kn]
+                            dist.scatter(x_sg[kn], x_all, src=0)
+                            ev_in[kn].record(comm)
+                    stream.wait_event(ev_in[k])
+                    out = model(x_sg[k], mask)
+                    ev_done[k].record(stream)
+                    flush.zero_()
+                    with torch.cuda.stream(comm):
+                        comm.wait_event(ev_done[k])
+                        dist.gather(out, out_all[k], dst=0)
+                        out.record_stream(comm)
+                stream.wait_stream(comm)
 
-            for _ in range(2):
-                sg_step()
+            sg_steps(2 * depth)
             torch.cuda.synchronize(dev)
             barrier()
             sg_start = torch.cuda.Event(enable_timing=True)
             sg_end = torch.cuda.Event(enable_timing=True)
             sg_start.record(stream)
-            for _ in range(args.steps):
-                sg_step()
-                flush.zero_()
+            sg_steps(args.steps)
             sg_end.record(stream)
             torch.cuda.synchronize(dev)
             barrier()
@@ -865,6 +900,8 @@ def main():
             "e2e": {"value": tokens / (e2e_max / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": x_cpu.numel() * 4 + mask_cpu.numel(),
                     "d2h_bytes_per_step": b * s * d * 4, "ms_per_step": e2e_max,
+                    "h2d_gbs_per_rank": (x_cpu.numel() * 4 + mask_cpu.numel()) / e2e_max / 1e6,
+                    "d2h_gbs_per_rank": b * s * d * 4 / e2e_max / 1e6,
                     "overlap": "uploads and downloads on two copy streams, 2 buffer sets; "
                                "L2 flush between forwards included"},
             "gpu_launches": int(round(launches_per_step * args.steps)),
@@ -878,7 +915,9 @@ def main():
                 "value": tokens / (sg_max / 1e3), "unit": "tokens/s", "ms_per_step": sg_max,
                 "bytes_per_step": 2 * (world - 1) * b * s * d * 4,
                 "note": "inputs start on GPU 0; per step NCCL scatter of the shards and "
-                        "gather of the outputs, max over ranks"}
+                        "gather of the outputs on a side stream, step i+1's scatter and "
+                        "step i's gather overlapping the forwards (two buffer sets); max "
+                        "over ranks"}
         if device_status != 0:
             print(json.dumps(line), flush=True)
             raise SystemExit(f"a kernel recorded device status {device_status} "

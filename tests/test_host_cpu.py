@@ -143,8 +143,9 @@ def test_plan_roundtrip_and_env(tmp_path, monkeypatch):
 
 
 def test_fused_layernorm_plan_selection(monkeypatch):
-    """The tuned B4 S4096 plan fuses the LayerNorms into the GEMMs, the
-    B8 S1024 one only the out-projection's; TJ_FUSE_LN=0/1 overrides."""
+    """The tuned B8 S1024 plan fuses only the out-projection's LayerNorm into
+    its GEMM; the B4 S4096 one keeps the LayerNorms standalone (faster there
+    since the persistent LayerNorm kernel); TJ_FUSE_LN=0/1 overrides."""
     from tjkernels import plans
     dev = torch.device("cuda")
     monkeypatch.delenv("TJ_IGNORE_PLANS", raising=False)
@@ -153,11 +154,14 @@ def test_fused_layernorm_plan_selection(monkeypatch):
     try:
         long_seq = (4, 4096, 1024, 16, 4096, 4, True, torch.float32, dev)
         p3 = plans.select_plan(*long_seq)
-        assert p3.fuse_layernorm and p3.fuse_layernorm_ffn
+        assert not p3.fuse_layernorm
         p2 = plans.select_plan(8, 1024, 1024, 16, 4096, 4, True, torch.float32, dev)
         assert p2.fuse_layernorm and not p2.fuse_layernorm_ffn
+        monkeypatch.setenv("TJ_FUSE_LN", "1")
+        assert plans.select_plan(*long_seq).fuse_layernorm
         monkeypatch.setenv("TJ_FUSE_LN", "0")
-        assert not plans.select_plan(*long_seq).fuse_layernorm
+        assert not plans.select_plan(8, 1024, 1024, 16, 4096, 4, True, torch.float32,
+                                     dev).fuse_layernorm
     finally:
         plans._cache = None
 

@@ -30,7 +30,10 @@ def K():
 # ------------------------------------------------------------------ LayerNorm
 
 @pytest.mark.parametrize("rows,d", [(1, 128), (37, 96), (256, 512), (1000, 768),
-                                    (513, 1024), (64, 4096), (8, 8192)])
+                                    (513, 1024), (64, 4096), (8, 8192),
+                                    # above 1024 rows with d <= 1024: the persistent
+                                    # warp-per-row kernel (several rows per warp)
+                                    (1025, 1024), (5500, 1024), (2049, 96), (40000, 512)])
 @pytest.mark.parametrize("delta_dtype", [None, torch.float32, torch.bfloat16, torch.float16])
 def test_add_layernorm(rows, d, delta_dtype):
     g = torch.Generator(device=DEV).manual_seed(rows * 7 + d)
@@ -49,13 +52,15 @@ def test_add_layernorm(rows, d, delta_dtype):
     assert ((out16.float() - ref).abs() <= 1e-2 * ref.abs() + 1e-2).all()
 
 
-def test_add_layernorm_row_mask_and_inplace():
-    rows, d = 300, 1024
+@pytest.mark.parametrize("rows", [300, 7000])
+@pytest.mark.parametrize("delta_dtype", [torch.float32, torch.float16])
+def test_add_layernorm_row_mask_and_inplace(rows, delta_dtype):
+    d = 1024
     res = torch.randn(rows, d, device=DEV)
-    delta = torch.randn(rows, d, device=DEV)
+    delta = torch.randn(rows, d, device=DEV).to(delta_dtype)
     w, b = torch.randn(d, device=DEV), torch.randn(d, device=DEV)
     mask = (torch.rand(rows, device=DEV) > 0.4).to(torch.uint8)
-    expect_res = res + delta
+    expect_res = res + delta.float()
     ref = F.layer_norm(expect_res, (d,), w, b, 1e-5)
     got_res, out = K().fused_add_layernorm(res, delta, w, b, 1e-5, out_dtype=torch.float32,
                                            row_mask=mask, residual_out=res)
@@ -87,6 +92,63 @@ def test_gemm_bias(m, n, k, dtype):
     assert out16.dtype == dtype
     tol = 2 ** -7 if dtype == torch.bfloat16 else 2 ** -10
     assert ((out16.double() - ref).abs() <= tol * ref.abs() + 1e-3 * scale).all()
+
+
+# Shapes that take the CTA-pair kernel (256 x 256 tiles over two CTAs): an
+# odd number of 128-row tiles (the last pair's second CTA has no rows), M
+# not a multiple of 128, N not a multiple of 256 (the peer's B half partly or
+# wholly past N), several rounds of the persistent grid.
+PAIR_SHAPES = [(1000, 3072, 1024), (4096, 4096, 1024), (5504, 3072, 1024), (1151, 2304, 768),
+               (3000, 1160, 512), (640, 1408, 1024), (16384, 1024, 256)]
+
+
+@pytest.mark.parametrize("m,n,k", PAIR_SHAPES)
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_gemm_cta_pair(m, n, k, dtype, monkeypatch):
+    """The CTA-pair GEMM against fp64 (fp32 and 16-bit output, with GELU), and
+    against the single-CTA kernel of the same shape (TJB_GEMM_PAIR=0), which
+    does the same products in the same order."""
+    g = torch.Generator(device=DEV).manual_seed(m + 3 * n + k)
+    a = torch.randn(m, k, device=DEV, generator=g).to(dtype)
+    w = (torch.randn(n, k, device=DEV, generator=g) / math.sqrt(k)).to(dtype)
+    bias = torch.randn(n, device=DEV, generator=g)
+    ref = a.double() @ w.double().T + bias.double()
+    scale = ref.abs().max().item() + 1e-6
+    monkeypatch.setenv("TJB_GEMM_PAIR", "1")
+    for _ in range(2):
+        out32 = K().gemm_bias(a, w, bias, out_dtype=torch.float32)
+        assert (out32.double() - ref).abs().max().item() <= 1e-5 * scale + 1e-5
+    out16 = K().gemm_bias(a, w, bias, act=K().ACT_GELU)
+    ref_g = F.gelu(ref, approximate="none")
+    tol = 2 ** -7 if dtype == torch.bfloat16 else 2 ** -10
+    assert ((out16.double() - ref_g).abs() <= tol * ref_g.abs() + 1e-3 * scale).all()
+    monkeypatch.setenv("TJB_GEMM_PAIR", "0")
+    single = K().gemm_bias(a, w, bias, out_dtype=torch.float32)
+    assert (out32 - single).abs().max().item() <= 1e-6 * scale
+
+
+@pytest.mark.parametrize("listed", [[0, 2, 3, 7], [1, 4, 6], [5]])
+def test_gemm_cta_pair_live_tiles(listed, monkeypatch):
+    """With a live-tile list each CTA of a pair takes one listed tile (an odd
+    count leaves the last pair's second CTA without rows); unlisted tiles are
+    not written."""
+    monkeypatch.setenv("TJB_GEMM_PAIR", "1")
+    m, n, k = 1000, 2048, 512
+    g = torch.Generator(device=DEV).manual_seed(len(listed))
+    a = torch.randn(m, k, device=DEV, generator=g).half()
+    w = (torch.randn(n, k, device=DEV, generator=g) / 16).half()
+    bias = torch.randn(n, device=DEV, generator=g)
+    tiles = torch.tensor([len(listed)] + listed + [0] * (8 - len(listed)), dtype=torch.int32,
+                         device=DEV)
+    out = torch.full((m, n), 7.0, dtype=torch.float32, device=DEV)
+    K().gemm_bias(a, w, bias, out_dtype=torch.float32, out=out, m_tiles=tiles)
+    ref = a.double() @ w.double().T + bias.double()
+    for t in range(8):
+        rows = slice(t * 128, min(t * 128 + 128, m))
+        if t in listed:
+            assert (out[rows].double() - ref[rows]).abs().max().item() < 1e-3
+        else:
+            assert (out[rows] == 7.0).all()
 
 
 # Stream-K runs for (5120, 1024, 4096), (5376, 1024, 3072) and (4480, 1032,
@@ -460,6 +522,33 @@ def test_gemm_and_layernorm_visit_only_listed_tiles():
         if t in listed:
             assert (h[rows] - ref_h[rows]).abs().max().item() < 1e-4
             assert torch.equal(new_res[rows], (res0 + delta)[rows])
+        else:
+            assert torch.equal(new_res[rows], res0[rows])
+
+
+def test_add_layernorm_live_tiles_many_rows():
+    """The persistent LayerNorm over a tile list of more than 1024 rows: listed
+    tiles (the ragged last one included) are normalised, the others are left
+    untouched."""
+    m, d = 9000, 1024  # 71 tiles, the last one 40 rows
+    listed = [0, 3, 4, 5, 17, 30, 31, 32, 50, 69, 70]
+    n_tiles = (m + 127) // 128
+    tiles = torch.tensor([len(listed)] + listed + [0] * (n_tiles - len(listed)),
+                         dtype=torch.int32, device=DEV)
+    g = torch.Generator(device=DEV).manual_seed(5)
+    res = torch.randn(m, d, device=DEV, generator=g)
+    delta = torch.randn(m, d, device=DEV, generator=g).half()
+    w, b = torch.randn(d, device=DEV, generator=g), torch.randn(d, device=DEV, generator=g)
+    res0 = res.clone()
+    new_res, h = K().fused_add_layernorm(res, delta, w, b, 1e-5, out_dtype=torch.float16,
+                                         residual_out=res, m_tiles=tiles)
+    x = res0 + delta.float()
+    ref = F.layer_norm(x, (d,), w, b, 1e-5)
+    for t in range(n_tiles):
+        rows = slice(t * 128, min(t * 128 + 128, m))
+        if t in listed:
+            assert ((h[rows].float() - ref[rows]).abs() <= 1e-2 * ref[rows].abs() + 1e-2).all()
+            assert torch.equal(new_res[rows], x[rows])
         else:
             assert torch.equal(new_res[rows], res0[rows])
 

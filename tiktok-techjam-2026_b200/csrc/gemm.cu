@@ -21,6 +21,7 @@
 // GEMMs whose tiles fill the SMs badly run stream-K (see kSkMinKBlocks): each
 // CTA takes an equal run of the tile-major k-block space and split tiles meet
 // in the workspace.
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -529,6 +530,343 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------------
+// CTA-pair form (tcgen05 cta_group::2): a cluster of two CTAs computes one
+// 256 x 256 output tile.  CTA r of the pair TMA-loads its own 128 rows of A
+// (the pair's 128-row tile 2p + r) and its own 128 rows of B (output
+// columns n*256 + 128r ..), each into its own shared memory, and both loads
+// count on the leader's stage barrier; the leader (rank 0) issues M=256,
+// N=256 MMAs that read both CTAs' tiles, and commits the stage release and
+// the accumulator-ready signal to both CTAs' barriers at once.  Each CTA's
+// tensor memory holds its own 128 rows x 256 columns, and its eight epilogue
+// warps store them exactly as the single-CTA kernel does, then count in on
+// the leader's accumulator-free barrier.  Per k-block a CTA loads 32 KB
+// instead of 48 KB for the same tensor work, a third less L2 -> shared
+// traffic, and its ring holds six stages.  No load is multicast.
+constexpr int kPairStages = 6;
+
+struct GemmPairCfg {
+  static constexpr uint32_t kABytes = kBM * kBK * 2;   // 128 rows of A
+  static constexpr uint32_t kBBytes = 128 * kBK * 2;   // this CTA's 128 rows of B
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kTmemCols = 512;           // two 256-column accumulators
+  static constexpr uint32_t kOutTile = 32 * 128;
+  static constexpr uint32_t kOutBytes = 8 * kOutTile;
+  static constexpr size_t kSmemBytes = 1024 + kPairStages * kStageBytes + kOutBytes + 256;
+};
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
+  using Cfg = GemmPairCfg;
+  constexpr int kStages = kPairStages;
+  constexpr int BN = 256;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kStages * Cfg::kABytes;
+  uint8_t* sOut = sB + kStages * Cfg::kBBytes;  // [epilogue warp][kOutTile]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + Cfg::kOutBytes);  // leader's are used
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 2;  // leader's are used
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0: the leader, which issues the MMAs
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);   // the leader's expect-tx arrival + both CTAs' bytes
+      mbar_init(&empty[s], 1);  // one multicast commit of the leader's MMAs
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 16);  // eight epilogue warps of each CTA
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    prefetch_tmap(&tmC);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  // Both CTAs' barriers are initialised and their tensor memory allocated
+  // before either signals the other.
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();
+  griddep_launch_dependents();
+  const int num_m = args.m_tiles != nullptr ? __ldg(args.m_tiles) : (args.M + kBM - 1) / kBM;
+  const int num_mp = (num_m + 1) / 2;
+  const int num_n = (args.N + BN - 1) / BN;
+  const int num_k = (args.K + kBK - 1) / kBK;
+  const int num_tiles = num_mp * num_n;
+  const int pair_id = static_cast<int>(blockIdx.x >> 1);
+  const int num_pairs = static_cast<int>(gridDim.x >> 1);
+  // This CTA's 128-row tile of pair tile (mp, .): 2 mp + rank.  A pair whose
+  // second tile does not exist loads the first one's rows again (the MMA
+  // needs both halves) and the peer stores nothing.
+  auto rows_of = [&](int mp, int& m_blk) {
+    int mt = 2 * mp + static_cast<int>(rank);
+    const bool has = mt < num_m;
+    if (!has) mt = 2 * mp;
+    m_blk = args.m_tiles != nullptr ? __ldg(args.m_tiles + 1 + mt) : mt;
+    return has;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      const uint32_t full_leader = map_to_rank(smem_u32(full), 0);
+      int stage = 0;
+      uint32_t phase = 0, issued = 0, last_parity = 0;
+      bool ok = true;
+      for (int t = pair_id; ok && t < num_tiles; t += num_pairs) {
+        int mp, n_blk, m_blk;
+        tile_coords(t, num_mp, num_n, mp, n_blk);
+        rows_of(mp, m_blk);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::kStageBytes);
+          const uint32_t bar = full_leader + static_cast<uint32_t>(stage) * 8u;
+          tma_load_2d_pair(sA + stage * Cfg::kABytes, &tmA, bar, kb * kBK, m_blk * kBM);
+          tma_load_2d_pair(sB + stage * Cfg::kBBytes, &tmB, bar, kb * kBK,
+                           n_blk * BN + static_cast<int>(rank) * 128);
+          issued |= 1u << stage;
+          last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Every load this CTA issued has landed once the MMAs that read it
+      // have released its stage (the loads count on the leader's barrier).
+      for (int s = 0; s < kStages; ++s)
+        if ((issued >> s) & 1u) mbar_wait_drain(&empty[s], (last_parity >> s) & 1u);
+    }
+  } else if (warp == 1) {
+    if (rank == 0) {
+      // ---------------------------------------------- MMA issuer (leader only)
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+      };
+      for (int t = pair_id; ok && t < num_tiles; t += num_pairs) {
+        if (!wait(&tempty[acc], acc_phase ^ 1)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!wait(&full[stage], phase)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * Cfg::kABytes);
+          const uint32_t b0 = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            umma_ss_pair_w(d_tmem, sdesc_sw128(a0 + k * 32, 16, 1024),
+                           sdesc_sw128(b0 + k * 32, 16, 1024), args.idesc,
+                           (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit_pair_w(&empty[stage], 0x3);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair_w(&tfull[acc], 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      umma_commit_pair_w(drain, 0x1);
+      mbar_wait_drain(drain, 0);
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    uint8_t* buf = sOut + (warp - 2) * Cfg::kOutTile;
+    const uint32_t tempty_leader = map_to_rank(smem_u32(tempty), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = pair_id; t < num_tiles; t += num_pairs) {
+      int mp, n_blk, m_blk;
+      tile_coords(t, num_mp, num_n, mp, n_blk);
+      const bool has_rows = rows_of(mp, m_blk);
+      bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const int row0 = m_blk * kBM + quad * 32;
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      auto emit = [&](const uint32_t (&w)[32], int col) {
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+        stage_row(buf, lane, w);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, buf, col, row0);
+          bulk_commit();
+        }
+      };
+      if (has_rows && args.out_dtype == TJB_F32) {
+#pragma unroll 1
+        for (int c = half; c < BN / 32; c += 2) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c * 32, r);
+          tmem_ld_wait(r);
+          const int col0 = n_blk * BN + c * 32;
+          if (col0 >= args.N) break;
+          float v[32];
+          bias_act(args, col0, r, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(v[i]);
+          emit(r, col0);
+        }
+      } else if (has_rows) {
+#pragma unroll 1
+        for (int c = half; c < BN / 64; c += 2) {
+          const int col0 = n_blk * BN + c * 64;
+          if (col0 >= args.N) break;
+          uint32_t w[32];
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t r[32];
+            tmem_ld32(taddr + c * 64 + hh * 32, r);
+            tmem_ld_wait(r);
+            float v[32];
+            bias_act(args, col0 + hh * 32, r, v);
+            if (args.out_dtype == TJB_BF16) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                w[hh * 16 + i] = Pack2<__nv_bfloat16>::pack(v[2 * i], v[2 * i + 1]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                w[hh * 16 + i] = Pack2<__half>::pack(v[2 * i], v[2 * i + 1]);
+            }
+          }
+          emit(w, col0);
+        }
+      }
+      // This warp is done reading the accumulator: count in on the leader.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader + static_cast<uint32_t>(acc) * 8u);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  // Neither CTA releases its tensor memory (or exits) while the leader's
+  // MMAs or the peer's epilogue may still touch the pair's resources.
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+std::mutex g_pair_mu;
+int g_pair_clusters[64] = {0};  // co-resident CTA pairs per device (0: not yet known)
+
+int launch_gemm_pair(const void* A, const void* B, const GemmArgs& args, int lda, int ldb,
+                     bool bf16, cudaStream_t stream) {
+  using Cfg = GemmPairCfg;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return TJB_ERR_NO_DEVICE;
+  int max_pairs = 0;
+  {
+    std::lock_guard<std::mutex> lock(g_pair_mu);
+    if (g_pair_clusters[dev] == 0) {
+      if (const int fs = cuda_status(cudaFuncSetAttribute(
+              gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+              static_cast<int>(Cfg::kSmemBytes))))
+        return fs;
+      // How many pairs fit at once (an SM pairs only within its cluster
+      // group, so this can be below half the SM count).
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * (num_sms() / 2));
+      cfg.blockDim = dim3(kGemmThreads);
+      cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (const int qs = cuda_status(cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel, &cfg)))
+        return qs;
+      g_pair_clusters[dev] = n > 0 ? n : -1;
+    }
+    max_pairs = g_pair_clusters[dev];
+  }
+  if (max_pairs <= 0) return TJB_ERR_LAUNCH;
+  CUtensorMap tmA, tmB;
+  const uint64_t dimA[2] = {static_cast<uint64_t>(args.K), static_cast<uint64_t>(args.M)};
+  const uint64_t strA[1] = {static_cast<uint64_t>(lda) * 2};
+  const uint32_t boxA[2] = {kBK, kBM};
+  const uint64_t dimB[2] = {static_cast<uint64_t>(args.K), static_cast<uint64_t>(args.N)};
+  const uint64_t strB[1] = {static_cast<uint64_t>(ldb) * 2};
+  const uint32_t boxB[2] = {kBK, 128};
+  int st = make_tmap_16bit(&tmA, 2, A, dimA, strA, boxA, bf16);
+  if (st != TJB_OK) return st;
+  st = make_tmap_16bit(&tmB, 2, B, dimB, strB, boxB, bf16);
+  if (st != TJB_OK) return st;
+  const int esz = args.out_dtype == TJB_F32 ? 4 : 2;
+  CUtensorMap tmC;
+  st = make_tmap_2d(&tmC, args.out_dtype, args.C, static_cast<uint64_t>(args.N),
+                    static_cast<uint64_t>(args.M), static_cast<uint64_t>(args.ldc) * esz,
+                    static_cast<uint32_t>(128 / esz), 32);
+  if (st != TJB_OK) return st;
+  const int num_m = (args.M + kBM - 1) / kBM;
+  const int pair_tiles = ((num_m + 1) / 2) * ((args.N + 255) / 256);
+  const int pairs = pair_tiles < max_pairs ? pair_tiles : max_pairs;
+  return launch_kernel_cluster(gemm_pair_kernel, dim3(2 * pairs), dim3(kGemmThreads),
+                               Cfg::kSmemBytes, stream, 2u, tmA, tmB, tmC, args);
+}
+
+// CTA pairs: TJB_GEMM_PAIR=0 keeps every GEMM on single CTAs and =1 uses
+// pairs wherever they apply (both for comparisons); unset, the tile choice
+// below decides.
+int pair_gemm_mode() {
+  const char* v = std::getenv("TJB_GEMM_PAIR");
+  if (v == nullptr || v[0] == '\0') return -1;
+  return v[0] == '0' ? 0 : 1;
+}
+
 std::mutex g_attr_mu;
 bool g_attr_done[64][3];
 
@@ -632,10 +970,19 @@ int gemm_impl(const void* A, const void* B, const float* bias, void* C, int M, i
     args.idesc = idesc_f16(kBM, 256, bf16, false);
     return launch_gemm<256>(A, B, args, lda, ldb, bf16, s);
   }
+  const int pair_mode = pair_gemm_mode();
+  if (pair_mode == 1 && N >= 256 && mt >= 2) {
+    args.idesc = idesc_f16(2 * kBM, 256, bf16, false);
+    return launch_gemm_pair(A, B, args, lda, ldb, bf16, s);
+  }
   const double c256 = N >= 256 ? static_cast<double>(waves(256)) : 1e30;
   const double c128 = N >= 128 ? waves(128) * 0.65 : 1e30;
   const double c64 = waves(64) * 0.5;
   if (c256 <= c128 && c256 <= c64) {
+    if (mt >= 2 && pair_mode != 0) {
+      args.idesc = idesc_f16(2 * kBM, 256, bf16, false);
+      return launch_gemm_pair(A, B, args, lda, ldb, bf16, s);
+    }
     args.idesc = idesc_f16(kBM, 256, bf16, false);
     return launch_gemm<256>(A, B, args, lda, ldb, bf16, s);
   }

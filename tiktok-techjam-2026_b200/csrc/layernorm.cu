@@ -179,6 +179,165 @@ __global__ void __launch_bounds__(kBlock) add_layernorm_kernel(
   }
 }
 
+// ------------------------------------------------------------------------
+// d <= 1024 over many rows: one warp per row, persistent.  Each warp walks
+// rows w, w + W, w + 2W, ... (W = warps in the grid) and issues the loads of
+// its next row before it reduces and stores the current one, so DRAM keeps
+// reading while the warp computes -- the one-row-per-warp kernel above puts
+// every warp of a wave in the same phase (all loading, then all storing).
+// kDelta: 0 no delta, 1 fp16, 2 bf16 (fp32 deltas would need 128 more
+// bytes of registers per row in flight; they take the kernel above).
+constexpr int kRowsMaxChunks = 8;  // 8 x 32 lanes x 4 columns = 1024
+
+template <int kDelta>
+struct RowLoad {
+  float4 res[kRowsMaxChunks];
+  // 16-bit deltas stay packed (8 bytes per chunk) until they are added.
+  uint2 dl[kDelta == 0 ? 1 : kRowsMaxChunks];
+};
+
+template <int kDelta>
+__device__ __forceinline__ void rows_load(RowLoad<kDelta>& L, const float* res, const void* delta,
+                                          int64_t row, int64_t rows, int d, int lane) {
+  const bool active = row < rows;
+  const int64_t base = row * d;
+#pragma unroll
+  for (int i = 0; i < kRowsMaxChunks; ++i) {
+    const int col = (i * 32 + lane) * 4;
+    if (active && col < d) {
+      L.res[i] = __ldcs(reinterpret_cast<const float4*>(res + base + col));
+      if constexpr (kDelta != 0) {
+        L.dl[i] = __ldcs(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(delta) + base + col));
+      }
+    }
+  }
+}
+
+template <int kDelta>
+__device__ __forceinline__ float4 rows_add(const RowLoad<kDelta>& L, int i) {
+  float4 v = L.res[i];
+  if constexpr (kDelta != 0) {
+    float2 a, b;
+    if constexpr (kDelta == 2) {
+      a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&L.dl[i].x));
+      b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&L.dl[i].y));
+    } else {
+      a = __half22float2(*reinterpret_cast<const __half2*>(&L.dl[i].x));
+      b = __half22float2(*reinterpret_cast<const __half2*>(&L.dl[i].y));
+    }
+    v.x += a.x;
+    v.y += a.y;
+    v.z += b.x;
+    v.w += b.y;
+  }
+  return v;
+}
+
+template <int kDelta>
+__device__ __forceinline__ void rows_finish(RowLoad<kDelta>& L, float* res_out, void* out,
+                                            const float4* sw, const float4* sb,
+                                            const uint8_t* __restrict__ row_mask, int64_t row,
+                                            int64_t rows, int d, float eps, int out_dtype,
+                                            int lane) {
+  if (row >= rows) return;  // warp-uniform
+  const int64_t base = row * d;
+  // Issued here so that its latency overlaps the reductions below.
+  const bool keep = row_mask == nullptr || __ldg(row_mask + row) != 0;
+  float4* v = L.res;  // the sum res + delta, in place
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < kRowsMaxChunks; ++i) {
+    const int col = (i * 32 + lane) * 4;
+    if (col < d) {
+      v[i] = rows_add(L, i);
+      sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float inv_d = 1.0f / static_cast<float>(d);
+  const float mean = sum * inv_d;
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < kRowsMaxChunks; ++i) {
+    const int col = (i * 32 + lane) * 4;
+    if (col < d) {
+      const float a = v[i].x - mean, bb = v[i].y - mean, c = v[i].z - mean, e = v[i].w - mean;
+      sq += (a * a + bb * bb) + (c * c + e * e);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  const float rstd = rsqrtf(sq * inv_d + eps);
+#pragma unroll
+  for (int i = 0; i < kRowsMaxChunks; ++i) {
+    const int col = (i * 32 + lane) * 4;
+    if (col < d) {
+      if (res_out != nullptr) *reinterpret_cast<float4*>(res_out + base + col) = v[i];
+      float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (keep) {
+        const float4 ww = sw[i * 32 + lane];
+        const float4 bb = sb[i * 32 + lane];
+        y.x = (v[i].x - mean) * rstd * ww.x + bb.x;
+        y.y = (v[i].y - mean) * rstd * ww.y + bb.y;
+        y.z = (v[i].z - mean) * rstd * ww.z + bb.z;
+        y.w = (v[i].w - mean) * rstd * ww.w + bb.w;
+      }
+      store_out4(out, out_dtype, base + col, y);
+    }
+  }
+}
+
+constexpr int kRowsBlock = 256;  // 8 warps
+
+template <int kDelta>
+__global__ void __launch_bounds__(kRowsBlock, 2) add_layernorm_rows_kernel(
+    const float* res, const void* __restrict__ delta, float* res_out, void* out,
+    const float* __restrict__ w, const float* __restrict__ b, int64_t rows, int d, float eps,
+    int out_dtype, const uint8_t* __restrict__ row_mask, const int32_t* __restrict__ m_tiles) {
+  // The LayerNorm weights are never written during a forward: staged in
+  // shared memory before the wait for the kernel that produces the rows.
+  __shared__ float4 sw[kRowsMaxChunks * 32], sb[kRowsMaxChunks * 32];
+  for (int c = threadIdx.x; c * 4 < d; c += kRowsBlock) {
+    sw[c] = __ldg(reinterpret_cast<const float4*>(w) + c);
+    sb[c] = __ldg(reinterpret_cast<const float4*>(b) + c);
+  }
+  __syncthreads();
+  griddep_wait();
+  griddep_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  // Row numbers fit 32 bits (the launcher checks rows < 2^31).
+  const int stride = static_cast<int>(gridDim.x) * (kRowsBlock / 32);
+  int i = static_cast<int>(blockIdx.x) * (kRowsBlock / 32) + (threadIdx.x >> 5);
+  // Rows are numbered over the live tiles when there is a list.
+  const int n = m_tiles != nullptr ? __ldg(m_tiles) * kTileRows : static_cast<int>(rows);
+  auto phys = [&](int v) -> int {
+    return m_tiles != nullptr ? __ldg(m_tiles + 1 + v / kTileRows) * kTileRows + v % kTileRows
+                              : v;
+  };
+  RowLoad<kDelta> A, B;
+  if (i >= n) return;
+  int ra = phys(i);
+  rows_load(A, res, delta, ra, rows, d, lane);
+  for (;;) {
+    int rb = 0;
+    if (i + stride < n) {
+      rb = phys(i + stride);
+      rows_load(B, res, delta, rb, rows, d, lane);
+    }
+    rows_finish(A, res_out, out, sw, sb, row_mask, ra, rows, d, eps, out_dtype, lane);
+    i += stride;
+    if (i >= n) return;
+    if (i + stride < n) {
+      ra = phys(i + stride);
+      rows_load(A, res, delta, ra, rows, d, lane);
+    }
+    rows_finish(B, res_out, out, sw, sb, row_mask, rb, rows, d, eps, out_dtype, lane);
+    i += stride;
+    if (i >= n) return;
+  }
+}
+
 }  // namespace
 }  // namespace tjb
 
@@ -211,6 +370,21 @@ extern "C" int tjb_add_layernorm_tiles(const float* res, const void* delta, floa
                          res_out, out, w, b, rows, d, eps, delta_dtype, out_dtype, row_mask,
                          m_tiles);
   };
+  if (d <= 1024 && !early && (delta == nullptr || delta_dtype != TJB_F32) &&
+      rows < (int64_t(1) << 31) - kTileRows) {
+    // Persistent warp-per-row form: at most two CTAs of eight warps per SM,
+    // and never more warps than rows.
+    const int64_t max_rows = m_tiles ? tiles * kTileRows : rows;
+    const int64_t blocks = (max_rows + kRowsBlock / 32 - 1) / (kRowsBlock / 32);
+    const int64_t grid = blocks < 2 * num_sms() ? blocks : 2 * num_sms();
+    auto run = [&](auto kern) {
+      return launch_kernel(kern, dim3(static_cast<unsigned>(grid)), dim3(kRowsBlock), 0, s, res,
+                           delta, res_out, out, w, b, rows, d, eps, out_dtype, row_mask, m_tiles);
+    };
+    if (delta == nullptr) return run(add_layernorm_rows_kernel<0>);
+    if (delta_dtype == TJB_F16) return run(add_layernorm_rows_kernel<1>);
+    if (delta_dtype == TJB_BF16) return run(add_layernorm_rows_kernel<2>);
+  }
   if (d <= 1024) {
     const int64_t grid = m_tiles ? tiles * (kTileRows / 8) : (rows + 7) / 8;
     return early ? go(add_layernorm_kernel<32, true>, grid) : go(add_layernorm_kernel<32, false>, grid);
