@@ -27,7 +27,6 @@
 // diagonal or a length boundary are masked.  With a prefix padding mask,
 // query tiles wholly past the sequence's valid length are skipped (their
 // rows are written as zeros) and keys stop at the valid length.
-#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -183,9 +182,7 @@ __device__ __forceinline__ bool pv_step(uint64_t* p_full, uint64_t* pv_done, uin
   return true;
 }
 
-// kTurns: the two softmax groups take turns at the exponentials (see the
-// softmax role below); without it they run them at the same time.
-template <int HD, bool kBF16, bool kTurns>
+template <int HD, bool kBF16>
 __global__ void __launch_bounds__(kPairThreads, 1)
     attn_pair_kernel(const __grid_constant__ CUtensorMap tm, const AttnArgs args) {
   using Cfg = PairCfg<HD>;
@@ -206,8 +203,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint64_t* p_full = s_free + 2;          // [group]
   uint64_t* pv_done = p_full + 2;         // [group]
   uint64_t* drain = pv_done + 2;                   // [issuer]
-  uint64_t* turn = drain + 2;                      // [group]: its turn at the exponentials
-  uint64_t* item_full = turn + 2;                  // [kItemSlots]
+  uint64_t* item_full = drain + 2;                 // [kItemSlots]
   uint64_t* item_empty = item_full + kItemSlots;   // [kItemSlots]
   volatile int* item_q = reinterpret_cast<volatile int*>(item_empty + kItemSlots);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_empty + kItemSlots) + kItemSlots;
@@ -233,8 +229,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     }
     mbar_init(&drain[0], 1);
     mbar_init(&drain[1], 1);
-    mbar_init(&turn[0], 4);  // the four warps of the other group
-    mbar_init(&turn[1], 4);
     for (int i = 0; i < kItemSlots; ++i) {
       mbar_init(&item_full[i], 1);
       mbar_init(&item_empty[i], 2 + 8);  // the two MMA warps and the eight softmax warps
@@ -407,21 +401,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const uint32_t o_col = Cfg::kOCol + g * HD;
     const float sl2 = args.scale_log2;
     const uint32_t p_col = Cfg::kPCol + g * Cfg::kPStride;
-    uint32_t t = 0;      // tiles this group has processed (all items)
-    uint32_t turns = 0;  // exponential phases this group has taken (kTurns)
+    uint32_t t = 0;  // tiles this group has processed (all items)
     bool ok = true;
-    // kTurns: the groups alternate at the exponentials, the MUFU-bound part
-    // of a step, so that one group's score load, row max, P store and
-    // barrier waits run while the other group's exponentials use the MUFU
-    // unit.  Without the alternation both groups reach those phases at the
-    // same time and the SM idles in between.  Group 0 goes first; each group
-    // takes one turn per key tile of the item's longer query tile (a tile it
-    // does not have is a turn passed on at once).  The turn barriers are
-    // mbarriers, so a stalled partner still ends in a bounded wait.
-    if (kTurns && g == 1) {
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&turn[0]);
-    }
     for (uint32_t qn = 0; ok; ++qn) {
       const uint32_t islot = qn % kItemSlots;
       if (!__all_sync(0xffffffffu, mbar_wait(&item_full[islot], (qn / kItemSlots) & 1, abort_flag)))
@@ -436,30 +417,19 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       uint16_t* out_ptr = static_cast<uint16_t*>(args.out) +
                           (static_cast<int64_t>(it.b) * args.S + qi) * args.ldo + it.h * HD;
       const int nk = it.n_kv[g];
-      if (nk == 0 && qi < args.S) {
+      if (nk == 0) {
+        if (qi < args.S) {
 #pragma unroll
-        for (int c = 0; c < HD / 8; ++c)
-          reinterpret_cast<uint4*>(out_ptr)[c] = make_uint4(0u, 0u, 0u, 0u);
+          for (int c = 0; c < HD / 8; ++c)
+            reinterpret_cast<uint4*>(out_ptr)[c] = make_uint4(0u, 0u, 0u, 0u);
+        }
+        continue;
       }
-      if (nk == 0 && !kTurns) continue;
-      const int rounds = kTurns ? max(it.n_kv[0], it.n_kv[1]) : nk;
       const uint8_t* km =
           use_key_mask ? args.key_mask + static_cast<int64_t>(it.b) * args.S : nullptr;
       float m_ref = -INFINITY;  // reference max the exponentials are taken against
       float l_i = 0.f;
-      for (int j = 0; j < rounds; ++j) {
-        if (kTurns && j >= nk) {
-          // No key tile of this group in this round: take the turn and pass
-          // it on at once.
-          if (!__all_sync(0xffffffffu, mbar_wait(&turn[g], turns & 1, abort_flag))) {
-            ok = false;
-            break;
-          }
-          ++turns;
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&turn[g ^ 1]);
-          continue;
-        }
+      for (int j = 0; j < nk; ++j) {
         bool w_ok = mbar_wait(&s_full[g], t & 1, abort_flag);
         if (!__all_sync(0xffffffffu, w_ok)) {
           ok = false;
@@ -514,13 +484,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           m_ref = m_new;
         }
         const float mb = m_ref == -INFINITY ? 0.f : m_ref * sl2;
-        if constexpr (kTurns) {
-          if (!__all_sync(0xffffffffu, mbar_wait(&turn[g], turns & 1, abort_flag))) {
-            ok = false;
-            break;
-          }
-          ++turns;
-        }
         // Exponentials into registers (64 packed pairs) before P is touched.
         // One pair in four goes to a polynomial on the FMA pipe, the rest to
         // the MUFU unit (measured at B4 S4096: 1/4 -> 468 TFLOP/s, 1/2 -> 448,
@@ -542,10 +505,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           }
           e[c] = kBF16 ? Pack2<__nv_bfloat16>::pack(p0, p1) : Pack2<__half>::pack(p0, p1);
         }
-        if constexpr (kTurns) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&turn[g ^ 1]);  // the other group's turn
-        }
         const float rowsum = (sa0 + sa1) + (sb0 + sb1);
         l_i += rowsum;
         // The previous PV has read P and accumulated into O: P is free and O
@@ -553,7 +512,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         // these scores were issued after that PV and commits complete in
         // order.
         if (!Cfg::kAlias && t >= 1) {
-          const bool w_ok = mbar_wait(&pv_done[g], (t - 1) & 1, abort_flag);
+          w_ok = mbar_wait(&pv_done[g], (t - 1) & 1, abort_flag);
           if (!__all_sync(0xffffffffu, w_ok)) {
             ok = false;
             break;
@@ -582,7 +541,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         ++t;
       }
       if (!ok) break;
-      if (nk == 0) continue;
       // Epilogue: O / l once the item's last PV has landed.
       const bool w_ok = mbar_wait(&pv_done[g], (t - 1) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, w_ok)) break;
@@ -630,13 +588,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   }
 }
 
-// The softmax groups alternate at the exponentials unless TJB_ATTN_TURNS=0
-// (kept for comparisons).
-bool attn_turns_enabled() {
-  const char* v = std::getenv("TJB_ATTN_TURNS");
-  return v == nullptr || v[0] != '0';
-}
-
 std::mutex g_pair_attr_mu;
 bool g_pair_attr_done[64][2];
 
@@ -649,8 +600,7 @@ int launch_attn_pair(const void* qkv, const AttnArgs& args, cudaStream_t stream)
     std::lock_guard<std::mutex> lock(g_pair_attr_mu);
     const int slot = HD == 64 ? 0 : 1;
     if (dev < 64 && !g_pair_attr_done[dev][slot]) {
-      for (auto fn : {attn_pair_kernel<HD, false, false>, attn_pair_kernel<HD, true, false>,
-                      attn_pair_kernel<HD, false, true>, attn_pair_kernel<HD, true, true>})
+      for (auto fn : {attn_pair_kernel<HD, false>, attn_pair_kernel<HD, true>})
         if (const int fs = cuda_status(cudaFuncSetAttribute(
                 fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                 static_cast<int>(Cfg::kSmemBytes))))
@@ -667,13 +617,10 @@ int launch_attn_pair(const void* qkv, const AttnArgs& args, cudaStream_t stream)
   if (st != TJB_OK) return st;
   const long total = static_cast<long>(args.B) * args.H * ((args.S + 2 * kTileQ - 1) / (2 * kTileQ));
   const int grid = static_cast<int>(total < num_sms() ? total : num_sms());
-  const bool turns = attn_turns_enabled();
-  auto go = [&](auto kern) {
-    return launch_kernel(kern, dim3(grid), dim3(kPairThreads), Cfg::kSmemBytes, stream, tm, args);
-  };
-  if (turns)
-    return args.bf16 ? go(attn_pair_kernel<HD, true, true>) : go(attn_pair_kernel<HD, false, true>);
-  return args.bf16 ? go(attn_pair_kernel<HD, true, false>) : go(attn_pair_kernel<HD, false, false>);
+  return args.bf16 ? launch_kernel(attn_pair_kernel<HD, true>, dim3(grid), dim3(kPairThreads),
+                                Cfg::kSmemBytes, stream, tm, args)
+                   : launch_kernel(attn_pair_kernel<HD, false>, dim3(grid), dim3(kPairThreads),
+                                Cfg::kSmemBytes, stream, tm, args);
 }
 
 }  // namespace
