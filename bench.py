@@ -97,7 +97,7 @@ CONFIG_NOTE = {
 METRIC = "forward tokens/sec"
 FLUSH_BYTES = 256 << 20
 
-# DRAM traffic of the dominant kernel (gemm_kernel) per launch, averaged over
+# DRAM traffic of the dominant kernel family (the tcgen05 GEMM) per launch, averaged over
 # the launches of one forward of the config's tuned plan: sum of
 # dram__bytes_read.sum + dram__bytes_write.sum over those launches / their
 # number, from one ncu capture of this bench's own command (a one-pass
@@ -848,8 +848,8 @@ def main():
         peaks = load_peaks()
         tokens = b * s * (1 if tp else world)
         value = tokens / (step_max / 1e3)
-        # The dominant kernel: gemm_kernel, launched by gemm_bias (one launch
-        # per call) and fused_ffn (two per call).
+        # The dominant kernel family: the tcgen05 GEMM (CTA-pair or single-CTA
+        # form), launched by gemm_bias (one launch per call) and fused_ffn (two).
         fams = [kern_plan[n] for n in ("gemm_bias", "fused_ffn") if n in kern_plan]
         gemm_ms = sum(v["ms_per_step"] for v in fams)
         gemm_flops = sum(v["flops_per_call"] * v["calls_per_step"] for v in fams)
@@ -875,7 +875,8 @@ def main():
                            plan=plan.to_json()),
             "roofline": {
                 "bound": "tensor",
-                "kernel": "gemm_kernel (tcgen05; every launch of it in the timed plan)",
+                "kernel": "tcgen05 GEMM: gemm_pair_kernel (CTA pairs) and gemm_kernel "
+                          "(single CTA, stream-K), every launch in the timed plan",
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak,
                 "peak_note": f"{peaks['source']} burst bf16/f16 dense (sustained "
@@ -883,9 +884,9 @@ def main():
                 "flops_per_launch": gemm_flops / gemm_launches,
                 "ms_per_launch": gemm_ms / gemm_launches,
                 "traffic": traffic,
-                "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum per launch of "
-                                "gemm_kernel, mean over one forward's launches, one ncu "
-                                "capture of this command" if traffic else None,
+                "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum per GEMM "
+                                "launch, mean over one forward's launches, one ncu capture "
+                                "of this command" if traffic else None,
                 "attn_tflops": rate("flash_attention"),
                 "attn_frac": frac(rate("flash_attention"), peak),
                 "ffn_tflops": rate("fused_ffn"), "ffn_frac": frac(rate("fused_ffn"), peak),
