@@ -268,7 +268,8 @@ class KernelTimer:
         for name, cost in (("gemm_bias", gemm_cost), ("fused_ffn", ffn_cost),
                            ("gemm_add_layernorm", gemm_cost),
                            ("fused_add_layernorm", ln_cost), ("flash_attention", attn_cost),
-                           ("mask_lengths", mask_cost), ("row_tiles", mask_cost)):
+                           ("mask_lengths", mask_cost), ("row_tiles", mask_cost),
+                           ("mask_lengths_tiles", mask_cost)):
             self._orig[name] = getattr(K, name)
             setattr(K, name, self._wrap(name, self._orig[name], cost))
         return self

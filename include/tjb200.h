@@ -276,6 +276,17 @@ int tjb_mask_lengths(const uint8_t* mask, int B, int S, int32_t* lengths,
                      int32_t* flags, tjb_stream_t stream);
 
 /*
+ * tjb_mask_lengths and tjb_row_tiles in one launch: lengths, the flag word
+ * and (tiles non-NULL) the live-tile list of tjb_row_tiles, all computed on
+ * the device with one CTA that classifies the rows in parallel.  Same
+ * outputs as the two calls in sequence.  Replaces Engine._mask_mode
+ * (tjkernels/engine.py:131-158) together with the tile listing, which has
+ * no counterpart in the reference.
+ */
+int tjb_mask_lengths_tiles(const uint8_t* mask, int B, int S, int32_t* lengths,
+                           int32_t* flags, int32_t* tiles, tjb_stream_t stream);
+
+/*
  * Live 128-row tiles of the flattened [B*S] token axis for a prefix padding
  * mask, on the device (no host synchronisation): a tile is live when it holds
  * a row (b, s) with s < round_up(lengths[b], 128) -- every valid row plus the

@@ -494,6 +494,49 @@ def test_row_tiles(b, s, lens):
     assert tiles[0] == n and tiles[1:1 + n] == list(range(n))
 
 
+def _mask_cases():
+    g = torch.Generator().manual_seed(5)
+    cases = []
+    for b, s in ((8, 1024), (3, 200), (5, 37), (2, 4096), (40, 512), (1, 1), (70, 64), (4, 16)):
+        lens = torch.randint(0, s + 1, (b,), generator=g)
+        lens[0] = s
+        if b > 1:
+            lens[1] = 0
+        prefix = torch.arange(s)[None, :] < lens[:, None]
+        holed = prefix.clone()
+        holed[b - 1, s // 2] = not holed[b - 1, s // 2]  # a 0 -> 1 rise, where S allows
+        if s > 2:
+            holed[b - 1, 0] = False
+            holed[b - 1, s - 1] = True
+        for m in (prefix, holed):
+            mi = m.to(torch.int)
+            rises = bool(((mi[:, 1:] == 1) & (mi[:, :-1] == 0)).any())
+            cases.append((m, not rises))
+    return cases
+
+
+@pytest.mark.parametrize("case", range(16))
+def test_mask_lengths_tiles_matches_separate_calls(case):
+    """The one-launch classification + tile listing equals tjb_mask_lengths
+    followed by tjb_row_tiles, for prefix masks and masks with a rise, S a
+    multiple of 16 (16-byte loads) or not, more rows than warps, empty rows;
+    and on a mask that does not start on a 16-byte boundary."""
+    mask, is_prefix = _mask_cases()[case]
+    for offset in (0, 3):
+        buf = torch.zeros(mask.numel() + offset, dtype=torch.uint8)
+        buf[offset:] = mask.flatten().to(torch.uint8)
+        m = buf.to(DEV)[offset:].view(mask.shape)
+        b, s = mask.shape
+        lens, flags = K().mask_lengths(m)
+        tiles = K().row_tiles(lens, flags, b, s, torch.device(DEV))
+        lens2, flags2, tiles2 = K().mask_lengths_tiles(m)
+        assert torch.equal(lens, lens2)
+        assert torch.equal(lens2.cpu(), mask.sum(-1).to(torch.int32))
+        assert (int(flags2) == 0) == is_prefix and (int(flags) == 0) == is_prefix
+        n = int(tiles[0])
+        assert int(tiles2[0]) == n and torch.equal(tiles[1:1 + n], tiles2[1:1 + n])
+
+
 def test_gemm_and_layernorm_visit_only_listed_tiles():
     m, n, k = 1000, 512, 256
     a = torch.randn(m, k, device=DEV).half()

@@ -208,6 +208,123 @@ __global__ void __launch_bounds__(1024) row_tiles_kernel(const int32_t* __restri
   if (threadIdx.x == 0) tiles[0] = s_base;
 }
 
+// ------------------------------------------- mask lengths + tiles, one pass
+// One CTA, one warp per row at a time (all rows in flight together, instead
+// of one row after another): each lane reads 16 mask bytes per step, counts
+// the non-zero ones and looks for a 0 -> 1 rise inside them and across the
+// boundary with the previous lane's last byte; then, in the same launch,
+// the live 128-row tiles are listed from the lengths just written (global
+// writes of the CTA are visible to all its threads after __syncthreads).
+__device__ __forceinline__ uint32_t nonzero_bytes(uint32_t w) {
+  // 0x01 in each byte of w that is non-zero.
+  return ((((w & 0x7F7F7F7Fu) + 0x7F7F7F7Fu) | w) >> 7) & 0x01010101u;
+}
+
+__global__ void __launch_bounds__(1024) mask_tiles_kernel(const uint8_t* __restrict__ mask,
+                                                          int B, int S,
+                                                          int32_t* lengths,
+                                                          int32_t* __restrict__ flags,
+                                                          int32_t* __restrict__ tiles) {
+  __shared__ int s_step;
+  __shared__ int s_warp[32];
+  __shared__ int s_base;
+  griddep_wait();
+  griddep_launch_dependents();
+  if (threadIdx.x == 0) {
+    s_step = 0;
+    s_base = 0;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps = static_cast<int>(blockDim.x >> 5);
+  const bool vec = (S % 16) == 0 && (reinterpret_cast<uintptr_t>(mask) & 15u) == 0;
+  for (int b = warp; b < B; b += nwarps) {
+    const uint8_t* row = mask + static_cast<int64_t>(b) * S;
+    int count = 0, step = 0;
+    if (vec) {
+      uint32_t carry = 1;  // "the byte before is non-zero": no rise at column 0
+      for (int j0 = 0; j0 < S; j0 += 32 * 16) {
+        const int j = j0 + lane * 16;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (j < S) v = __ldg(reinterpret_cast<const uint4*>(row + j));
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t nz[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) nz[i] = nonzero_bytes(w[i]);
+        // The byte before this lane's first byte: the previous lane's last.
+        const uint32_t last = (nz[3] >> 24) & 1u;
+        uint32_t prev = __shfl_up_sync(0xffffffffu, last, 1);
+        if (lane == 0) prev = carry;
+        carry = __shfl_sync(0xffffffffu, last, 31);
+        if (j < S) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            count += __popc(nz[i]);
+            // Byte k of the word rises when it is non-zero and byte k - 1 (or
+            // the carried byte for k = 0) is zero.
+            const uint32_t before = (nz[i] << 8) | prev;
+            step |= (nz[i] & ~before) != 0u;
+            prev = nz[i] >> 24;
+          }
+        }
+      }
+    } else {
+      for (int j = lane; j < S; j += 32) {
+        const int v = row[j] != 0;
+        count += v;
+        if (j > 0 && v && row[j - 1] == 0) step = 1;
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      count += __shfl_xor_sync(0xffffffffu, count, o);
+      step |= __shfl_xor_sync(0xffffffffu, step, o);
+    }
+    if (lane == 0) {
+      lengths[b] = count;
+      if (step) s_step = 1;
+    }
+  }
+  __syncthreads();
+  const int any_step = s_step;
+  if (threadIdx.x == 0) *flags = any_step ? TJB_ERR_NON_PREFIX_MASK : 0;
+  if (tiles == nullptr) return;  // uniform
+  // Live tiles, exactly as row_tiles_kernel lists them.
+  const int64_t T = static_cast<int64_t>(B) * S;
+  const int n_tiles = static_cast<int>((T + 127) / 128);
+  for (int t0 = 0; t0 < n_tiles; t0 += blockDim.x) {
+    const int t = t0 + threadIdx.x;
+    int live = 0;
+    if (t < n_tiles) {
+      if (any_step) {
+        live = 1;
+      } else {
+        const int64_t r0 = static_cast<int64_t>(t) * 128;
+        const int64_t r1 = min(r0 + 128, T);
+        for (int64_t bb = r0 / S; bb * S < r1 && !live; ++bb) {
+          const int64_t first = max(r0, bb * S) - bb * S;
+          const int len = min(max(lengths[bb], 0), S);
+          const int64_t reach = (static_cast<int64_t>(len) + 127) / 128 * 128;
+          if (first < reach) live = 1;
+        }
+      }
+    }
+    const unsigned ballot = __ballot_sync(0xffffffffu, live);
+    const int in_warp = __popc(ballot & ((1u << lane) - 1u));
+    if (lane == 0) s_warp[warp] = __popc(ballot);
+    __syncthreads();
+    int before = 0, total = 0;
+    for (int w = 0; w < nwarps; ++w) {
+      if (w < warp) before += s_warp[w];
+      total += s_warp[w];
+    }
+    if (live) tiles[1 + s_base + before + in_warp] = t;
+    __syncthreads();
+    if (threadIdx.x == 0) s_base += total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) tiles[0] = s_base;
+}
+
 // --------------------------------------------------------- bounded-wait test
 __global__ void selftest_wait_kernel(const int32_t* flag, int64_t timeout_ns) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
@@ -280,6 +397,15 @@ int tjb_mask_lengths(const uint8_t* mask, int B, int S, int32_t* lengths, int32_
   if (!tjb::device_ok()) return TJB_ERR_NO_DEVICE;
   return tjb::launch_kernel(tjb::mask_lengths_kernel, dim3(1), dim3(1024), 0,
                          reinterpret_cast<cudaStream_t>(stream), mask, B, S, lengths, flags);
+}
+
+int tjb_mask_lengths_tiles(const uint8_t* mask, int B, int S, int32_t* lengths, int32_t* flags,
+                           int32_t* tiles, tjb_stream_t stream) {
+  if (!mask || !lengths || !flags || B <= 0 || S <= 0) return TJB_ERR_INVALID_ARGUMENT;
+  if (!tjb::device_ok()) return TJB_ERR_NO_DEVICE;
+  return tjb::launch_kernel(tjb::mask_tiles_kernel, dim3(1), dim3(1024), 0,
+                            reinterpret_cast<cudaStream_t>(stream), mask, B, S, lengths, flags,
+                            tiles);
 }
 
 int tjb_row_tiles(const int32_t* lengths, const int32_t* flags, int B, int S, int32_t* tiles,

@@ -55,6 +55,7 @@ SIGNATURES = {
     "tjb_ffn_noalloc": (_c_int, [_p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int,
                                  _c_int, _p]),
     "tjb_mask_lengths": (_c_int, [_p, _c_int, _c_int, _p, _p, _p]),
+    "tjb_mask_lengths_tiles": (_c_int, [_p, _c_int, _c_int, _p, _p, _p, _p]),
     "tjb_device_status": (_c_int, [_c_int]),
     "tjb_device_status_async": (_c_int, [_p, _p]),
     "tjb_selftest_wait": (_c_int, [_p, _c_i64, _p]),

@@ -244,9 +244,10 @@ class Engine:
         if mask is not None:
             mask_u8 = mask.contiguous().view(torch.uint8) if mask.dtype == torch.bool \
                 else (mask != 0).to(torch.uint8)
-            lengths, flags = K.mask_lengths(mask_u8)
             if plan.skip_padding:
-                tiles = K.row_tiles(lengths, flags, batch, seq, x.device)
+                lengths, flags, tiles = K.mask_lengths_tiles(mask_u8)
+            else:
+                lengths, flags = K.mask_lengths(mask_u8)
 
         res = x.reshape(tokens, d)
         if res.dtype != torch.float32 or not res.is_contiguous():

@@ -305,6 +305,22 @@ def mask_lengths(mask: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     return lengths, flags
 
 
+def mask_lengths_tiles(mask: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """``mask_lengths`` and ``row_tiles`` from one launch (tjb_mask_lengths_tiles):
+    ``(lengths, flags, tiles)``, all on the device, no host sync."""
+    _need_cuda(mask)
+    if mask.dtype == torch.bool:
+        mask = mask.contiguous().view(torch.uint8)
+    b, s = mask.shape
+    lengths = torch.empty((b,), dtype=torch.int32, device=mask.device)
+    flags = torch.empty((1,), dtype=torch.int32, device=mask.device)
+    tiles = torch.empty((1 + (b * s + 127) // 128,), dtype=torch.int32, device=mask.device)
+    status = _lib.lib().tjb_mask_lengths_tiles(_ptr(mask), b, s, _ptr(lengths), _ptr(flags),
+                                               _ptr(tiles), _stream(mask.device))
+    _lib.check(status, "tjb_mask_lengths_tiles")
+    return lengths, flags, tiles
+
+
 def row_tiles(lengths: Optional[torch.Tensor], flags: Optional[torch.Tensor], batch: int,
               seq: int, device: torch.device) -> torch.Tensor:
     """Device-side list of live 128-row tiles of the [B*S] token axis:
@@ -339,6 +355,7 @@ __all__ = [
     "gemm_add_layernorm", "gemm_add_layernorm_supports",
     "fused_ffn",
     "ffn_single_kernel", "ffn_fused_supports",
-    "flash_attention", "flash_supports", "mask_lengths", "row_tiles", "device_status",
+    "flash_attention", "flash_supports", "mask_lengths", "mask_lengths_tiles", "row_tiles",
+    "device_status",
     "device_status_async",
 ]
