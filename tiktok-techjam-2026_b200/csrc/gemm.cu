@@ -975,14 +975,22 @@ int gemm_impl(const void* A, const void* B, const float* bias, void* C, int M, i
     args.idesc = idesc_f16(2 * kBM, 256, bf16, false);
     return launch_gemm_pair(A, B, args, lda, ldb, bf16, s);
   }
+  // CTA pairs: waves of 256 x 256 pair tiles over half the SMs, each pair
+  // tile costing 0.9 of a single-CTA 128 x 256 tile (measured on B200 at the
+  // configs' shapes: M5504 N3072 K1024 36.9 vs 40.0 us, M5504 N1024 K1024
+  // 25.6 vs 28.6 us against the 128-wide tile this model picked before).
+  const bool pair_ok = mt >= 2 && N >= 256 && pair_mode != 0;
+  const long pair_tiles = ((mt + 1) / 2) * ((N + 255) / 256);
+  const long pair_slots = sms / 2 > 0 ? sms / 2 : 1;
+  const double cpair = pair_ok ? ((pair_tiles + pair_slots - 1) / pair_slots) * 0.9 : 1e30;
   const double c256 = N >= 256 ? static_cast<double>(waves(256)) : 1e30;
   const double c128 = N >= 128 ? waves(128) * 0.65 : 1e30;
   const double c64 = waves(64) * 0.5;
+  if (cpair <= c256 && cpair <= c128 && cpair <= c64) {
+    args.idesc = idesc_f16(2 * kBM, 256, bf16, false);
+    return launch_gemm_pair(A, B, args, lda, ldb, bf16, s);
+  }
   if (c256 <= c128 && c256 <= c64) {
-    if (mt >= 2 && pair_mode != 0) {
-      args.idesc = idesc_f16(2 * kBM, 256, bf16, false);
-      return launch_gemm_pair(A, B, args, lda, ldb, bf16, s);
-    }
     args.idesc = idesc_f16(kBM, 256, bf16, false);
     return launch_gemm<256>(A, B, args, lda, ldb, bf16, s);
   }
