@@ -151,14 +151,17 @@ def test_gemm_cta_pair_live_tiles(listed, monkeypatch):
             assert (out[rows] == 7.0).all()
 
 
-# Stream-K runs for (5120, 1024, 4096), (5376, 1024, 3072) and (4480, 1032,
-# 4096) (a partial last column tile); its small-M form for (64, 768, 3072),
+# Stream-K on CTA pairs for (5120, 1024, 4096), (5376, 1024, 3072), (4480,
+# 1032, 4096) (a partial last column tile), (5504, 1024, 4096) (an odd
+# number of row tiles: the last pair's second CTA has no rows of its own)
+# and (2816, 2048, 4096); its single-CTA small-M form for (64, 768, 3072),
 # (128, 1024, 4096) and (100, 200, 2048); the other shapes (among them
 # (9600, 1024, 4096): more than two waves) take the whole-tile path with a
 # workspace passed.
 SPLIT_SHAPES = [(5120, 1024, 1024), (5120, 1024, 4096), (5376, 1024, 3072), (9600, 1024, 4096),
-                (4480, 1032, 4096), (64, 768, 3072), (128, 1024, 4096), (100, 200, 2048),
-                (4608, 3072, 1024), (300, 136, 512), (2000, 1032, 2048), (129, 64, 64)]
+                (4480, 1032, 4096), (5504, 1024, 4096), (2816, 2048, 4096), (64, 768, 3072),
+                (128, 1024, 4096), (100, 200, 2048), (4608, 3072, 1024), (300, 136, 512),
+                (2000, 1032, 2048), (129, 64, 64)]
 
 
 @pytest.mark.parametrize("m,n,k", SPLIT_SHAPES)

@@ -625,6 +625,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     m_blk = args.m_tiles != nullptr ? __ldg(args.m_tiles + 1 + mt) : mt;
     return has;
   };
+  // Stream-K over pair tiles (see kSkMinKBlocks), with each CTA of a pair
+  // writing its own 128 rows of a split tile's partial into its own slot.
+  bool sk = false;
+  int sk_w = 0;  // k-blocks per pair's run
+  if (args.ws != nullptr && static_cast<int>(gridDim.x) <= kSkMaxPartials) {
+    const int rem = num_tiles % num_pairs;
+    if (num_k >= kSkMinKBlocks && rem != 0 && 4 * (num_pairs - rem) >= 3 * num_pairs &&
+        2 * num_tiles >= num_pairs && num_tiles < 2 * num_pairs) {
+      sk = true;
+      sk_w = (num_tiles * num_k + num_pairs - 1) / num_pairs;
+    }
+  }
+  auto pieces = [&]() {
+    PieceIter it;
+    it.num_k = num_k;
+    it.num_tiles = num_tiles;
+    it.stride = num_pairs;
+    it.sk = sk;
+    it.cursor = sk ? pair_id * sk_w : pair_id;
+    it.end = sk ? min((pair_id + 1) * sk_w, num_tiles * num_k) : 0;
+    return it;
+  };
 
   if (warp == 0) {
     if (lane == 0) {
@@ -633,11 +655,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0, issued = 0, last_parity = 0;
       bool ok = true;
-      for (int t = pair_id; ok && t < num_tiles; t += num_pairs) {
+      PieceIter pit = pieces();
+      GemmPiece un;
+      while (ok && pit.next(un)) {
         int mp, n_blk, m_blk;
-        tile_coords(t, num_mp, num_n, mp, n_blk);
+        tile_coords(un.tile, num_mp, num_n, mp, n_blk);
         rows_of(mp, m_blk);
-        for (int kb = 0; kb < num_k; ++kb) {
+        for (int kb = un.kb0; kb < un.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
             ok = false;
             break;
@@ -669,11 +693,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       auto wait = [&](uint64_t* bar, uint32_t parity) {
         return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
       };
-      for (int t = pair_id; ok && t < num_tiles; t += num_pairs) {
+      PieceIter pit = pieces();
+      GemmPiece un;
+      while (ok && pit.next(un)) {
         if (!wait(&tempty[acc], acc_phase ^ 1)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < num_k; ++kb) {
+        for (int kb = un.kb0; kb < un.kb1; ++kb) {
           if (!wait(&full[stage], phase)) {
             ok = false;
             break;
@@ -685,7 +711,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int k = 0; k < kBK / 16; ++k)
             umma_ss_pair_w(d_tmem, sdesc_sw128(a0 + k * 32, 16, 1024),
                            sdesc_sw128(b0 + k * 32, 16, 1024), args.idesc,
-                           (kb > 0 || k > 0) ? 1u : 0u);
+                           (kb > un.kb0 || k > 0) ? 1u : 0u);
           umma_commit_pair_w(&empty[stage], 0x3);
           if (++stage == kStages) {
             stage = 0;
@@ -710,9 +736,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t tempty_leader = map_to_rank(smem_u32(tempty), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = pair_id; t < num_tiles; t += num_pairs) {
+    PieceIter pit = pieces();
+    GemmPiece un;
+    while (pit.next(un)) {
       int mp, n_blk, m_blk;
-      tile_coords(t, num_mp, num_n, mp, n_blk);
+      tile_coords(un.tile, num_mp, num_n, mp, n_blk);
       const bool has_rows = rows_of(mp, m_blk);
       bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
@@ -721,6 +749,54 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int row0 = m_blk * kBM + quad * 32;
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      // Stream-K roles as in the single-CTA kernel, per pair: a piece that
+      // starts past k-block 0 is a contributor, one that starts at 0 and
+      // stops short of the end the owner; pairs pair_id + 1 .. c_last hold
+      // the rest of the owner's tile, and CTA r of the owner reads the slot
+      // of CTA r of each of them (blockIdx 2p + r: the same 128 rows).
+      const bool contributor = un.kb0 > 0;
+      const bool owner = un.kb0 == 0 && un.kb1 < num_k;
+      const int c_last = owner ? ((un.tile + 1) * num_k - 1) / sk_w : 0;
+      auto partial_at = [&](int p, int j) {
+        return args.ws + (static_cast<int64_t>(p) * 256 + j) * kBM + quad * 32 + lane;
+      };
+      if (contributor) {
+#pragma unroll 1
+        for (int c = half; c < BN / 32; c += 2) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c * 32, r);
+          tmem_ld_wait(r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            __stcg(partial_at(blockIdx.x, c * 32 + i), __uint_as_float(r[i]));
+        }
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(args.ws_flags + blockIdx.x, 1);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(tempty_leader + static_cast<uint32_t>(acc) * 8u);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+        continue;
+      }
+      if (owner) {
+        // Each contributor CTA's eight epilogue warps have counted in.
+        if (lane == 0)
+          for (int p = pair_id + 1; p <= c_last; ++p)
+            wait_count(args.ws_flags + 2 * p + static_cast<int>(rank), 8, abort_flag);
+        __syncwarp();
+      }
+      auto add_partials = [&](uint32_t (&r)[32], int c0) {
+        for (int p = pair_id + 1; p <= c_last; ++p) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            r[i] = __float_as_uint(__uint_as_float(r[i]) +
+                                   __ldcg(partial_at(2 * p + static_cast<int>(rank), c0 + i)));
+        }
+      };
       auto emit = [&](const uint32_t (&w)[32], int col) {
         if (lane == 0) bulk_wait_read<0>();
         __syncwarp();
@@ -740,6 +816,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tmem_ld_wait(r);
           const int col0 = n_blk * BN + c * 32;
           if (col0 >= args.N) break;
+          if (owner) add_partials(r, c * 32);
           float v[32];
           bias_act(args, col0, r, v);
 #pragma unroll
@@ -757,6 +834,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             uint32_t r[32];
             tmem_ld32(taddr + c * 64 + hh * 32, r);
             tmem_ld_wait(r);
+            if (owner) add_partials(r, c * 64 + hh * 32);
             float v[32];
             bias_act(args, col0 + hh * 32, r, v);
             if (args.out_dtype == TJB_BF16) {
@@ -771,6 +849,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           emit(w, col0);
         }
+      }
+      if (owner) {
+        // The last of this CTA's eight warps to have read every partial
+        // returns the contributors' counters to zero (see gemm_kernel).
+        __syncwarp();
+        if (lane == 0)
+          for (int p = pair_id + 1; p <= c_last; ++p) {
+            const int slot = 2 * p + static_cast<int>(rank);
+            if (atomicAdd(args.ws_flags + kSkMaxPartials + slot, 1) == 7) {
+              atomicExch(args.ws_flags + slot, 0);
+              atomicExch(args.ws_flags + kSkMaxPartials + slot, 0);
+            }
+          }
       }
       // This warp is done reading the accumulator: count in on the leader.
       tc_fence_before();
@@ -965,12 +1056,23 @@ int gemm_impl(const void* A, const void* B, const float* bias, void* C, int M, i
   // live-tile list M is an upper bound and the kernel decides again).
   const long mt = (M + kBM - 1) / kBM;
   auto waves = [&](int bn) { return (mt * ((N + bn - 1) / bn) + sms - 1) / sms; };
+  const int pair_mode = pair_gemm_mode();
+  // Stream-K on CTA pairs where the pair tiles make one to two waves over
+  // the pairs: the pair tile's lighter operand traffic and the balanced
+  // k-block runs together (the kernel decides again from the live tiles).
+  const long sk_pair_tiles = ((mt + 1) / 2) * ((N + 255) / 256);
+  const long sk_pairs = sms / 2 > 0 ? sms / 2 : 1;
+  if (workspace != nullptr && pair_mode != 0 && mt >= 2 && N >= 256 &&
+      (K + kBK - 1) / kBK >= kSkMinKBlocks && 2 * sk_pair_tiles >= sk_pairs &&
+      sk_pair_tiles < 2 * sk_pairs) {
+    args.idesc = idesc_f16(2 * kBM, 256, bf16, false);
+    return launch_gemm_pair(A, B, args, lda, ldb, bf16, s);
+  }
   if (workspace != nullptr && N >= 256 && (K + kBK - 1) / kBK >= kSkMinKBlocks &&
       2 * mt * ((N + 255) / 256) >= sms && mt * ((N + 255) / 256) < 2 * sms) {
     args.idesc = idesc_f16(kBM, 256, bf16, false);
     return launch_gemm<256>(A, B, args, lda, ldb, bf16, s);
   }
-  const int pair_mode = pair_gemm_mode();
   if (pair_mode == 1 && N >= 256 && mt >= 2) {
     args.idesc = idesc_f16(2 * kBM, 256, bf16, false);
     return launch_gemm_pair(A, B, args, lda, ldb, bf16, s);
