@@ -332,6 +332,54 @@ int tjb_device_status(int clear);
  */
 int tjb_device_status_async(int32_t* host_dst, tjb_stream_t stream);
 
+/* One encoder block's parameters for tjb_forward_small (device pointers):
+ * the nn.Linear weights [out, in] in the compute dtype, biases and
+ * LayerNorm parameters fp32. */
+typedef struct {
+  const void* wqkv;  /* [3d, d]: Wq; Wk; Wv stacked */
+  const void* wo;    /* [d, d] */
+  const void* w1;    /* [F, d] */
+  const void* w2;    /* [d, F] */
+  const float* bqkv; /* [3d] */
+  const float* bo;   /* [d] */
+  const float* b1;   /* [F] */
+  const float* b2;   /* [d] */
+  const float* ln1_w;
+  const float* ln1_b;
+  const float* ln2_w;
+  const float* ln2_b;
+  float ln1_eps;
+  float ln2_eps;
+} tjb_small_layer;
+
+/* Workspace bytes tjb_forward_small needs for B sequences of S tokens. */
+size_t tjb_forward_small_workspace_bytes(int B, int S, int d, int F);
+
+/*
+ * The whole encoder forward of a small batch in one launch:
+ *   out = final_LN(blocks(x)), x and out fp32 [B*S, d]; valid (device
+ *   uint8 [B*S], or NULL for all valid) marks padded tokens with 0: they
+ *   are left out as keys and their output rows are written as zero (the
+ *   reference's key-padding mask and masked_fill).
+ * Pre-LN blocks as in tjb_add_layernorm / tjb_gemm_bias / tjb_flash_fwd
+ * (residual stream fp32, LayerNorm statistics fp32, GEMM operands in the
+ * compute dtype with fp32 accumulation, softmax in fp32), causal or not.
+ * layers: host array of L (<= 12) blocks.  Needs B*S <= 256 tokens,
+ * S <= 128, head_dim 64 (d = 64 H), d and F multiples of 128, d <= 1280,
+ * dtype TJB_F16.  workspace: tjb_forward_small_workspace_bytes(B, S, d, F)
+ * bytes, 16-byte aligned, zero before its first use and then left to this
+ * function (its first 8 bytes hold the grid barrier: calls that may overlap
+ * need separate workspaces; after TJB_ERR_DEVICE_TIMEOUT zero it again).
+ * A cooperative launch of one CTA per SM runs the forward as phases
+ * separated by bounded grid barriers.  Replaces, for small batches, the
+ * per-layer launch sequence of the engine's forward (tjkernels/engine.py:
+ * 205-269 in the reference), whose launches it fuses into one.
+ */
+int tjb_forward_small(const tjb_small_layer* layers, int L, const float* lnf_w,
+                      const float* lnf_b, float lnf_eps, const float* x, float* out,
+                      const uint8_t* valid, int B, int S, int d, int H, int F, int causal,
+                      int dtype, void* workspace, size_t workspace_bytes, tjb_stream_t stream);
+
 /*
  * Self-test of the bounded device-side wait: one thread spins on *flag
  * (device int32) until it becomes non-zero or timeout_ns elapses; on timeout

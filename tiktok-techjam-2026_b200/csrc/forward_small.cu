@@ -1,0 +1,718 @@
+// forward_small.cu -- the whole encoder forward of a small batch (at most
+// 256 tokens, head_dim 64) in one persistent cooperative kernel.
+//
+// At a few dozen tokens every GEMM of the block is a weight stream: each
+// weight is used by at most 256 tokens, and a launch per op spends most of
+// its time starting, filling its pipeline and draining.  Here one grid (one
+// CTA per SM, co-resident by a cooperative launch) runs the forward as a
+// sequence of phases separated by grid barriers (a counter and a generation
+// word in global memory, every wait bounded):
+//
+//   per layer  LN1 (+ the previous FFN-out's split-K partials, bias, residual)
+//              QKV GEMM -> qkv            attention -> ctx
+//              out-projection GEMM, split over K -> fp32 partials
+//              LN2 (+ those partials, bias, residual)
+//              FFN-in GEMM + bias + erf-GELU -> hidden
+//              FFN-out GEMM, split over K -> fp32 partials
+//   then       final LayerNorm (+ the last partials), padded rows written as 0
+//
+// GEMMs are swapped so that the weights fill the MMA's M side: a work unit
+// is 128 output features x all (padded) tokens x a range of k-blocks;
+// warp 0 TMA-loads the weight tile (128 x 64) and the activation tile
+// (tokens x 64, both K-major, 128-byte swizzle) into a 4-stage ring, warp 1
+// issues tcgen05.mma (M=128, N=tokens, K=16) into one of two TMEM
+// accumulators, and warps 2-9 read it back (one feature per TMEM lane, 32
+// tokens per load) and store 32 consecutive features of a token per warp
+// instruction.  The out-projection and FFN-out have few output features
+// (d / 128 tiles), so their k-blocks are split over the grid and the next
+// LayerNorm phase adds the partials in a fixed order.  Attention (a sequence
+// of at most 128 tokens) runs on the CUDA cores in fp32, a CTA per (sequence,
+// head, 32 query rows).  Activations stay in L2 between phases.
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace tjb {
+namespace {
+
+constexpr int kFsThreads = 320;   // producer warp, MMA warp, eight epilogue warps
+constexpr int kFsMaxLayers = 12;
+constexpr int kFsMaxTokens = 256;
+constexpr int kFsMaxSeq = 128;    // attention keeps a sequence's K and V in shared memory
+constexpr int kFsHead = 64;
+constexpr int kFsStages = 4;
+constexpr int kFsQRows = 32;      // query rows per attention unit
+
+struct FsLayer {
+  const float* ln1_w;
+  const float* ln1_b;
+  const float* bqkv;
+  const float* bo;
+  const float* ln2_w;
+  const float* ln2_b;
+  const float* b1;
+  const float* b2;
+  float ln1_eps, ln2_eps;
+};
+
+struct FsArgs {
+  // Weights (A operands, [out, in] K-major) and activations (B operands,
+  // [tokens, K] K-major): 128-byte-swizzled 64-column boxes.
+  CUtensorMap w_qkv[kFsMaxLayers], w_o[kFsMaxLayers], w_1[kFsMaxLayers], w_2[kFsMaxLayers];
+  CUtensorMap x_h, x_ctx, x_h2, x_hidden;
+  FsLayer layer[kFsMaxLayers];
+  const float* lnf_w;
+  const float* lnf_b;
+  float lnf_eps;
+  const float* x;           // [T, d] input
+  float* out;               // [T, d] output
+  const uint8_t* valid;     // [T]: 0 marks a padded token (masked key, zero output row), or null
+  float* res;               // [T, d] residual stream
+  uint16_t* h;              // [T, d] LN1 output
+  uint16_t* qkv;            // [T, 3d]
+  uint16_t* ctx;            // [T, d]
+  uint16_t* h2;             // [T, d] LN2 output
+  uint16_t* hidden;         // [T, F]
+  float* part;              // [split][T][d] split-K partials
+  unsigned* bar;            // [2]: arrivals, generation (the generation never resets)
+  int B, S, T, Tpad, d, H, F, L;
+  int causal, bf16;
+  int ks_o, ks_2;           // k-splits of the out-projection and FFN-out
+  uint32_t idesc;
+  float scale_log2;         // softmax scale * log2(e)
+};
+
+struct FsSmem {
+  static constexpr uint32_t kABytes = 128 * 64 * 2;
+  static constexpr uint32_t kBBytes = kFsMaxTokens * 64 * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr size_t kRing = static_cast<size_t>(kFsStages) * kStageBytes;
+  static constexpr size_t kBytes = 1024 + kRing + 1024;
+};
+
+__device__ __forceinline__ unsigned fs_ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Grid-wide barrier number `k` (1, 2, ...) of this launch; gen0 is the
+// generation word read at entry.  Bounded: false once the wait exceeds
+// kWaitTimeoutNs (the status word records it) or another CTA gave up.
+__device__ __forceinline__ bool fs_grid_sync(unsigned* bar, unsigned gen0, unsigned k,
+                                             volatile int* abort_flag) {
+  // Generic-proxy writes of this phase (global activations, and the
+  // attention tiles in the shared ring) are ordered before the next phase's
+  // TMA (async-proxy) accesses.
+  fence_proxy_async_global();
+  fence_proxy_async_smem();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned target = gen0 + k;
+    if (atomicAdd(&bar[0], 1u) == gridDim.x - 1) {
+      atomicExch(&bar[0], 0u);
+      __threadfence();
+      atomicExch(&bar[1], target);
+    } else {
+      const uint64_t t0 = globaltimer();
+      while (static_cast<int>(fs_ld_acquire_u32(&bar[1]) - target) < 0) {
+        if (globaltimer() - t0 > kWaitTimeoutNs) {
+          record_status(TJB_ERR_DEVICE_TIMEOUT);
+          *abort_flag = 1;
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+    __threadfence();
+  }
+  __syncthreads();
+  fence_proxy_async_global();
+  return *abort_flag == 0;
+}
+
+// Ring and accumulator positions; every role keeps its own copy and moves
+// only the fields it owns, across all GEMM phases of the launch.
+struct FsRing {
+  int stage = 0;
+  uint32_t phase = 0;
+  int acc = 0;
+  uint32_t acc_phase = 0;
+  uint32_t issued = 0, last_parity = 0;  // producer: stages with a load, its parity
+};
+
+struct FsShared {
+  uint8_t* sA;
+  uint8_t* sB;
+  uint64_t* full;
+  uint64_t* empty;
+  uint64_t* tfull;
+  uint64_t* tempty;
+  uint32_t tmem_base;
+  volatile int* abort_flag;
+};
+
+// One GEMM phase: out[t][n] over N output features (weights [N, K]) and the
+// padded tokens, K a multiple of 64, N of 128.  Units (feature tile nt,
+// k-split kc) go to the CTAs in turn.  ks == 1: out16 = act(acc + bias) in
+// 16-bit [T, N]; ks > 1: part[kc][T][N] = acc (fp32, no bias).
+__device__ __forceinline__ void fs_gemm(const FsArgs& a, const CUtensorMap* tmW,
+                                        const CUtensorMap* tmX, int N, int K, int ks,
+                                        const float* bias, int act, uint16_t* out16, float* part,
+                                        const FsShared& sh, FsRing& ring) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kb_total = K / 64;
+  const int kbu = (kb_total + ks - 1) / ks;
+  const int units = (N / 128) * ks;
+  auto unit_range = [&](int u, int& nt, int& kc, int& kb0, int& kb1) {
+    nt = u / ks;
+    kc = u - nt * ks;
+    kb0 = kc * kbu;
+    kb1 = min(kb_total, kb0 + kbu);
+  };
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t tx = FsSmem::kABytes + static_cast<uint32_t>(a.Tpad) * 128u;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+        int nt, kc, kb0, kb1;
+        unit_range(u, nt, kc, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&sh.empty[ring.stage], ring.phase ^ 1, sh.abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&sh.full[ring.stage], tx);
+          tma_load_2d(sh.sA + ring.stage * FsSmem::kABytes, tmW, &sh.full[ring.stage], kb * 64,
+                      nt * 128);
+          tma_load_2d(sh.sB + ring.stage * FsSmem::kBBytes, tmX, &sh.full[ring.stage], kb * 64, 0);
+          ring.issued |= 1u << ring.stage;
+          ring.last_parity = (ring.last_parity & ~(1u << ring.stage)) | (ring.phase << ring.stage);
+          if (++ring.stage == kFsStages) {
+            ring.stage = 0;
+            ring.phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, sh.abort_flag));
+    };
+    bool ok = true;
+    for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+      int nt, kc, kb0, kb1;
+      unit_range(u, nt, kc, kb0, kb1);
+      if (kb0 >= kb1) continue;
+      if (!wait(&sh.tempty[ring.acc], ring.acc_phase ^ 1)) break;
+      tc_fence_after();
+      const uint32_t d_tmem = sh.tmem_base + static_cast<uint32_t>(ring.acc * kFsMaxTokens);
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!wait(&sh.full[ring.stage], ring.phase)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sh.sA + ring.stage * FsSmem::kABytes);
+        const uint32_t b0 = smem_u32(sh.sB + ring.stage * FsSmem::kBBytes);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_ss_w(d_tmem, sdesc_sw128(a0 + k * 32, 16, 1024), sdesc_sw128(b0 + k * 32, 16, 1024),
+                    a.idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+        umma_commit_w(&sh.empty[ring.stage]);
+        if (++ring.stage == kFsStages) {
+          ring.stage = 0;
+          ring.phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      umma_commit_w(&sh.tfull[ring.acc]);
+      if (++ring.acc == 2) {
+        ring.acc = 0;
+        ring.acc_phase ^= 1;
+      }
+    }
+  } else {
+    const int quad = warp & 3;         // TMEM lanes (features) this warp may read
+    const int half = (warp - 2) >> 2;  // which token chunks
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      int nt, kc, kb0, kb1;
+      unit_range(u, nt, kc, kb0, kb1);
+      if (kb0 >= kb1) continue;
+      if (!__all_sync(0xffffffffu, mbar_wait(&sh.tfull[ring.acc], ring.acc_phase, sh.abort_flag)))
+        break;
+      tc_fence_after();
+      const int n = nt * 128 + quad * 32 + lane;  // this thread's output feature
+      const uint32_t taddr = sh.tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                             static_cast<uint32_t>(ring.acc * kFsMaxTokens);
+      const float bn = ks == 1 && bias != nullptr ? __ldg(bias + n) : 0.f;
+#pragma unroll 1
+      for (int c = half; c * 32 < a.T; c += 2) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c * 32, r);
+        tmem_ld_wait(r);
+        if (ks == 1) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int t = c * 32 + i;
+            float v = __uint_as_float(r[i]) + bn;
+            if (act) v = gelu_erf(v);
+            if (t < a.T) out16[static_cast<int64_t>(t) * N + n] = __half_as_ushort(__float2half_rn(v));
+          }
+        } else {
+          float* dst = part + static_cast<int64_t>(kc) * a.T * N + n;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int t = c * 32 + i;
+            if (t < a.T) __stcg(dst + static_cast<int64_t>(t) * N, __uint_as_float(r[i]));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.tempty[ring.acc]);
+      if (++ring.acc == 2) {
+        ring.acc = 0;
+        ring.acc_phase ^= 1;
+      }
+    }
+  }
+}
+
+// Attention, fp32 on the CUDA cores: a unit is (sequence b, head hh, 32
+// query rows); K and V rows [0, keys) of the head go to shared memory (K
+// padded to 65 floats a row, so lane j's key j reads conflict-free), eight
+// warps take four query rows each: lane j scores keys j, j + 32, ... (keys
+// after the row when causal, and padded keys, are left out), the row's max
+// and sum meet by shuffles, and lane j accumulates output dimensions 2j and
+// 2j + 1.  A row with no key left is written as zero.
+__device__ __forceinline__ void fs_attention(const FsArgs& a, float* sm) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_qb = (a.S + kFsQRows - 1) / kFsQRows;
+  const int units = a.B * a.H * n_qb;
+  const int ld = 3 * a.d;  // qkv row length
+  float* sK = sm;                          // [kFsMaxSeq][65]
+  float* sV = sK + kFsMaxSeq * 65;         // [kFsMaxSeq][64]
+  float* sQ = sV + kFsMaxSeq * kFsHead;    // [32][64]
+  for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    const int qb = u % n_qb;
+    const int bh = u / n_qb;
+    const int b = bh / a.H, hh = bh - (bh / a.H) * a.H;
+    const int q0 = qb * kFsQRows, q1 = min(a.S, q0 + kFsQRows);
+    const int keys = a.causal ? q1 : a.S;
+    const uint8_t* vk = a.valid != nullptr ? a.valid + static_cast<int64_t>(b) * a.S : nullptr;
+    const uint16_t* base = a.qkv + static_cast<int64_t>(b) * a.S * ld;
+    __syncthreads();  // the previous unit is done with the shared tiles
+    for (int idx = threadIdx.x; idx < keys * 32; idx += kFsThreads) {
+      const int r = idx >> 5, c2 = (idx & 31) * 2;
+      const uint16_t* row = base + static_cast<int64_t>(r) * ld + hh * kFsHead + c2;
+      const __half2 k2 = *reinterpret_cast<const __half2*>(row + a.d);
+      const __half2 v2 = *reinterpret_cast<const __half2*>(row + 2 * a.d);
+      sK[r * 65 + c2] = __low2float(k2);
+      sK[r * 65 + c2 + 1] = __high2float(k2);
+      sV[r * kFsHead + c2] = __low2float(v2);
+      sV[r * kFsHead + c2 + 1] = __high2float(v2);
+    }
+    for (int idx = threadIdx.x; idx < (q1 - q0) * 32; idx += kFsThreads) {
+      const int r = idx >> 5, c2 = (idx & 31) * 2;
+      const __half2 q2 = *reinterpret_cast<const __half2*>(
+          base + static_cast<int64_t>(q0 + r) * ld + hh * kFsHead + c2);
+      sQ[r * kFsHead + c2] = __low2float(q2);
+      sQ[r * kFsHead + c2 + 1] = __high2float(q2);
+    }
+    __syncthreads();
+    if (warp >= 8) continue;
+    for (int rr = 0; rr < kFsQRows / 8; ++rr) {
+      const int i = q0 + warp * (kFsQRows / 8) + rr;
+      if (i >= q1) break;
+      const int lim = a.causal ? i + 1 : a.S;  // keys [0, lim), less the padded ones
+      uint32_t* dst = reinterpret_cast<uint32_t*>(
+          a.ctx + (static_cast<int64_t>(b) * a.S + i) * a.d + hh * kFsHead + 2 * lane);
+      const float* q = sQ + (i - q0) * kFsHead;
+      float s[kFsMaxSeq / 32];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int m = 0; m < kFsMaxSeq / 32; ++m) {
+        const int j = lane + 32 * m;
+        s[m] = -INFINITY;
+        if (j < lim && (vk == nullptr || vk[j] != 0)) {
+          const float* k = sK + j * 65;
+          float dot = 0.f;
+#pragma unroll 16
+          for (int e = 0; e < kFsHead; ++e) dot = fmaf(q[e], k[e], dot);
+          s[m] = dot;
+          mx = fmaxf(mx, dot);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float sum = 0.f;
+#pragma unroll
+      for (int m = 0; m < kFsMaxSeq / 32; ++m) {
+        s[m] = s[m] != -INFINITY ? exp2f((s[m] - mx) * a.scale_log2) : 0.f;
+        sum += s[m];
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      float o0 = 0.f, o1 = 0.f;
+#pragma unroll
+      for (int m = 0; m < kFsMaxSeq / 32; ++m) {
+        if (32 * m >= lim) break;
+        for (int jj = 0; jj < 32; ++jj) {
+          const int j = 32 * m + jj;
+          const float p = __shfl_sync(0xffffffffu, s[m], jj);
+          if (j < lim) {
+            o0 = fmaf(p, sV[j * kFsHead + 2 * lane], o0);
+            o1 = fmaf(p, sV[j * kFsHead + 2 * lane + 1], o1);
+          }
+        }
+      }
+      const float inv = sum > 0.f ? 1.f / sum : 0.f;
+      const __half2 r2 = __floats2half2_rn(o0 * inv, o1 * inv);
+      *dst = *reinterpret_cast<const uint32_t*>(&r2);
+    }
+  }
+}
+
+// Block-wide sum over the CTA's 320 threads (red: 16 floats of shared
+// memory, reused after the return).
+__device__ __forceinline__ float fs_block_sum(float v, float* red) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();  // red is free (its last readers are past this point)
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < kFsThreads / 32; ++w) t += red[w];
+  return t;
+}
+
+// Rows t of v = in[t] (+ the ks split-K partials and bias, in order kc = 0,
+// 1, ...): res_out[t] = v (if given); then LayerNorm(v) * w + bb in fp32
+// statistics, to h16 (16-bit) or to out32 with rows past their sequence's
+// length written as zero.  A CTA per row, thread i owning columns i, i +
+// 320, ... (d <= 1280).
+__device__ __forceinline__ void fs_layernorm(const FsArgs& a, const float* in, const float* part,
+                                             int ks, const float* bias, float* res_out,
+                                             uint16_t* h16, float* out32, const float* w,
+                                             const float* bb, float eps, float* red) {
+  const int d = a.d;
+  const float inv_d = 1.f / static_cast<float>(d);
+  for (int t = blockIdx.x; t < a.T; t += gridDim.x) {
+    float v[4];
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int j = threadIdx.x + kFsThreads * c;
+      v[c] = 0.f;
+      if (j < d) {
+        float x = in[static_cast<int64_t>(t) * d + j];
+        if (part != nullptr) {
+          for (int kc = 0; kc < ks; ++kc)
+            x += __ldcg(part + (static_cast<int64_t>(kc) * a.T + t) * d + j);
+          x += __ldg(bias + j);
+        }
+        v[c] = x;
+        s += x;
+      }
+    }
+    const float mean = fs_block_sum(s, red) * inv_d;
+    float sq = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int j = threadIdx.x + kFsThreads * c;
+      if (j < d) sq += (v[c] - mean) * (v[c] - mean);
+    }
+    const float rstd = rsqrtf(fs_block_sum(sq, red) * inv_d + eps);
+    const bool valid = a.valid == nullptr || a.valid[t] != 0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int j = threadIdx.x + kFsThreads * c;
+      if (j >= d) continue;
+      const int64_t at = static_cast<int64_t>(t) * d + j;
+      if (res_out != nullptr) res_out[at] = v[c];
+      const float y = (v[c] - mean) * rstd * __ldg(w + j) + __ldg(bb + j);
+      if (h16 != nullptr)
+        h16[at] = __half_as_ushort(__float2half_rn(y));
+      else
+        out32[at] = valid ? y : 0.f;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kFsThreads, 1) forward_small_kernel(const __grid_constant__ FsArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  FsShared sh;
+  sh.sA = smem;
+  sh.sB = smem + kFsStages * FsSmem::kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + FsSmem::kRing);
+  sh.full = bars;
+  sh.empty = bars + kFsStages;
+  sh.tfull = sh.empty + kFsStages;
+  sh.tempty = sh.tfull + 2;
+  uint64_t* drain = sh.tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  sh.abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile unsigned* gen_slot = reinterpret_cast<volatile unsigned*>(tmem_slot + 2);
+  float* red = reinterpret_cast<float*>(tmem_slot + 4);  // [16]
+  const int warp = threadIdx.x >> 5;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kFsStages; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sh.tfull[b], 1);
+      mbar_init(&sh.tempty[b], 8);
+    }
+    mbar_init(drain, 1);
+    *sh.abort_flag = 0;
+    // Every CTA reads the generation before it first arrives, so none can
+    // see a barrier of this launch completed already.
+    *gen_slot = fs_ld_acquire_u32(a.bar + 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * kFsMaxTokens);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  sh.tmem_base = *tmem_slot;
+  const unsigned gen0 = *gen_slot;
+  unsigned k = 0;
+  FsRing ring;
+  const int d = a.d;
+  float* sm = reinterpret_cast<float*>(smem);  // attention tiles reuse the idle ring
+
+  for (int l = 0; l < a.L; ++l) {
+    const FsLayer& ly = a.layer[l];
+    if (l == 0)
+      fs_layernorm(a, a.x, nullptr, 0, nullptr, a.res, a.h, nullptr, ly.ln1_w, ly.ln1_b,
+                   ly.ln1_eps, red);
+    else
+      fs_layernorm(a, a.res, a.part, a.ks_2, a.layer[l - 1].b2, a.res, a.h, nullptr, ly.ln1_w,
+                   ly.ln1_b, ly.ln1_eps, red);
+    if (!fs_grid_sync(a.bar, gen0, ++k, sh.abort_flag)) goto done;
+    fs_gemm(a, &a.w_qkv[l], &a.x_h, 3 * d, d, 1, ly.bqkv, 0, a.qkv, nullptr, sh, ring);
+    if (!fs_grid_sync(a.bar, gen0, ++k, sh.abort_flag)) goto done;
+    fs_attention(a, sm);
+    if (!fs_grid_sync(a.bar, gen0, ++k, sh.abort_flag)) goto done;
+    fs_gemm(a, &a.w_o[l], &a.x_ctx, d, d, a.ks_o, nullptr, 0, nullptr, a.part, sh, ring);
+    if (!fs_grid_sync(a.bar, gen0, ++k, sh.abort_flag)) goto done;
+    fs_layernorm(a, a.res, a.part, a.ks_o, ly.bo, a.res, a.h2, nullptr, ly.ln2_w, ly.ln2_b,
+                 ly.ln2_eps, red);
+    if (!fs_grid_sync(a.bar, gen0, ++k, sh.abort_flag)) goto done;
+    fs_gemm(a, &a.w_1[l], &a.x_h2, a.F, d, 1, ly.b1, 1, a.hidden, nullptr, sh, ring);
+    if (!fs_grid_sync(a.bar, gen0, ++k, sh.abort_flag)) goto done;
+    fs_gemm(a, &a.w_2[l], &a.x_hidden, d, a.F, a.ks_2, nullptr, 0, nullptr, a.part, sh, ring);
+    if (!fs_grid_sync(a.bar, gen0, ++k, sh.abort_flag)) goto done;
+  }
+  fs_layernorm(a, a.res, a.part, a.ks_2, a.layer[a.L - 1].b2, nullptr, nullptr, a.out, a.lnf_w,
+               a.lnf_b, a.lnf_eps, red);
+
+done:
+  // After an abort: the loads this CTA's producer issued land and its MMAs
+  // retire before the shared and tensor memory are released.
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kFsStages; ++s)
+      if ((ring.issued >> s) & 1u) mbar_wait_drain(&sh.full[s], (ring.last_parity >> s) & 1u);
+  }
+  if (warp == 1) {
+    umma_commit_w(drain);
+    mbar_wait_drain(drain, 0);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(sh.tmem_base, 2 * kFsMaxTokens);
+  }
+}
+
+std::mutex g_fs_mu;
+bool g_fs_attr_done[64];
+
+
+// Workspace layout (each part 256-byte aligned): barrier words, res, h,
+// qkv, ctx, h2, hidden, split-K partials.
+struct FsLayout {
+  size_t bar, res, h, qkv, ctx, h2, hidden, part, total;
+  int ks_o, ks_2;
+};
+
+size_t fs_align(size_t v) { return (v + 255) / 256 * 256; }
+
+// k-split of a GEMM with N output features and K: as many units as CTAs at
+// most, every split non-empty.
+int fs_split(int N, int K, int grid) {
+  const int nt = N / 128, kb = K / 64;
+  const int want = std::max(1, std::min(kb, grid / std::max(nt, 1)));
+  const int kbu = (kb + want - 1) / want;
+  return (kb + kbu - 1) / kbu;
+}
+
+FsLayout fs_layout(int T, int d, int F, int grid) {
+  FsLayout L;
+  L.ks_o = fs_split(d, d, grid);
+  L.ks_2 = fs_split(d, F, grid);
+  size_t at = 0;
+  auto take = [&](size_t bytes) {
+    const size_t here = at;
+    at += fs_align(bytes);
+    return here;
+  };
+  const size_t t = static_cast<size_t>(T);
+  L.bar = take(256);
+  L.res = take(t * d * 4);
+  L.h = take(t * d * 2);
+  L.qkv = take(t * 3 * d * 2);
+  L.ctx = take(t * d * 2);
+  L.h2 = take(t * d * 2);
+  L.hidden = take(t * F * 2);
+  L.part = take(static_cast<size_t>(std::max(L.ks_o, L.ks_2)) * t * d * 4);
+  L.total = at;
+  return L;
+}
+
+}  // namespace
+}  // namespace tjb
+
+extern "C" size_t tjb_forward_small_workspace_bytes(int B, int S, int d, int F) {
+  using namespace tjb;
+  if (B <= 0 || S <= 0 || d <= 0 || F <= 0) return 0;
+  return fs_layout(B * S, d, F, num_sms()).total;
+}
+
+extern "C" int tjb_forward_small(const tjb_small_layer* layers, int L, const float* lnf_w,
+                                 const float* lnf_b, float lnf_eps, const float* x, float* out,
+                                 const uint8_t* valid, int B, int S, int d, int H, int F,
+                                 int causal, int dtype, void* workspace, size_t workspace_bytes,
+                                 tjb_stream_t stream) {
+  using namespace tjb;
+  if (!layers || !lnf_w || !lnf_b || !x || !out || !workspace || L <= 0 || B <= 0 || S <= 0)
+    return TJB_ERR_INVALID_ARGUMENT;
+  if (dtype != TJB_F16) return TJB_ERR_UNSUPPORTED_DTYPE;
+  const int T = B * S;
+  if (L > kFsMaxLayers || T > kFsMaxTokens || S > kFsMaxSeq || H <= 0 || H * kFsHead != d ||
+      d % 128 != 0 || F % 128 != 0 || d > 4 * kFsThreads)
+    return TJB_ERR_BAD_SHAPE;
+  if (!device_ok()) return TJB_ERR_NO_DEVICE;
+  const int grid = num_sms();
+  const FsLayout lay = fs_layout(T, d, F, grid);
+  if (workspace_bytes < lay.total || !aligned16(workspace)) return TJB_ERR_INVALID_ARGUMENT;
+  if (!aligned16(x) || !aligned16(out)) return TJB_ERR_BAD_ALIGNMENT;
+  for (int l = 0; l < L; ++l) {
+    const tjb_small_layer& ly = layers[l];
+    if (!ly.wqkv || !ly.wo || !ly.w1 || !ly.w2 || !ly.bqkv || !ly.bo || !ly.b1 || !ly.b2 ||
+        !ly.ln1_w || !ly.ln1_b || !ly.ln2_w || !ly.ln2_b)
+      return TJB_ERR_INVALID_ARGUMENT;
+    if (!aligned16(ly.wqkv) || !aligned16(ly.wo) || !aligned16(ly.w1) || !aligned16(ly.w2))
+      return TJB_ERR_BAD_ALIGNMENT;
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(g_fs_mu);
+    if (dev < 64 && !g_fs_attr_done[dev]) {
+      if (const int fs = cuda_status(cudaFuncSetAttribute(
+              forward_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+              static_cast<int>(FsSmem::kBytes))))
+        return fs;
+      g_fs_attr_done[dev] = true;
+    }
+  }
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  FsArgs a;
+  memset(&a, 0, sizeof(a));
+  a.H = H;
+  const int Tpad = (T + 15) / 16 * 16;
+  auto wmap = [&](CUtensorMap* m, const void* w, int rows, int K) {
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(rows)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(K) * 2};
+    const uint32_t box[2] = {64, 128};
+    return make_tmap_16bit(m, 2, w, dims, strides, box, false);
+  };
+  auto xmap = [&](CUtensorMap* m, const void* p, int K) {
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(T)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(K) * 2};
+    const uint32_t box[2] = {64, static_cast<uint32_t>(Tpad)};
+    return make_tmap_16bit(m, 2, p, dims, strides, box, false);
+  };
+  for (int l = 0; l < L; ++l) {
+    const tjb_small_layer& ly = layers[l];
+    int st = wmap(&a.w_qkv[l], ly.wqkv, 3 * d, d);
+    if (st == TJB_OK) st = wmap(&a.w_o[l], ly.wo, d, d);
+    if (st == TJB_OK) st = wmap(&a.w_1[l], ly.w1, F, d);
+    if (st == TJB_OK) st = wmap(&a.w_2[l], ly.w2, d, F);
+    if (st != TJB_OK) return st;
+    FsLayer& fl = a.layer[l];
+    fl.ln1_w = ly.ln1_w;
+    fl.ln1_b = ly.ln1_b;
+    fl.bqkv = ly.bqkv;
+    fl.bo = ly.bo;
+    fl.ln2_w = ly.ln2_w;
+    fl.ln2_b = ly.ln2_b;
+    fl.b1 = ly.b1;
+    fl.b2 = ly.b2;
+    fl.ln1_eps = ly.ln1_eps;
+    fl.ln2_eps = ly.ln2_eps;
+  }
+  a.h = reinterpret_cast<uint16_t*>(ws + lay.h);
+  a.ctx = reinterpret_cast<uint16_t*>(ws + lay.ctx);
+  a.h2 = reinterpret_cast<uint16_t*>(ws + lay.h2);
+  a.hidden = reinterpret_cast<uint16_t*>(ws + lay.hidden);
+  int st = xmap(&a.x_h, a.h, d);
+  if (st == TJB_OK) st = xmap(&a.x_ctx, a.ctx, d);
+  if (st == TJB_OK) st = xmap(&a.x_h2, a.h2, d);
+  if (st == TJB_OK) st = xmap(&a.x_hidden, a.hidden, F);
+  if (st != TJB_OK) return st;
+  a.lnf_w = lnf_w;
+  a.lnf_b = lnf_b;
+  a.lnf_eps = lnf_eps;
+  a.x = x;
+  a.out = out;
+  a.valid = valid;
+  a.res = reinterpret_cast<float*>(ws + lay.res);
+  a.qkv = reinterpret_cast<uint16_t*>(ws + lay.qkv);
+  a.part = reinterpret_cast<float*>(ws + lay.part);
+  a.bar = reinterpret_cast<unsigned*>(ws + lay.bar);
+  a.B = B;
+  a.S = S;
+  a.T = T;
+  a.d = d;
+  a.Tpad = Tpad;
+  a.F = F;
+  a.L = L;
+  a.causal = causal;
+  a.bf16 = 0;
+  a.ks_o = lay.ks_o;
+  a.ks_2 = lay.ks_2;
+  a.idesc = idesc_f16(128, Tpad, false, false);
+  a.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(kFsHead));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kFsThreads);
+  cfg.dynamicSmemBytes = FsSmem::kBytes;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, forward_small_kernel, a));
+}

@@ -7,3 +7,4 @@
 #include "attention.cu"
 #include "ffn.cu"
 #include "ffn_fused.cu"
+#include "forward_small.cu"

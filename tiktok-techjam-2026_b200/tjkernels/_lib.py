@@ -59,7 +59,19 @@ SIGNATURES = {
     "tjb_device_status": (_c_int, [_c_int]),
     "tjb_device_status_async": (_c_int, [_p, _p]),
     "tjb_selftest_wait": (_c_int, [_p, _c_i64, _p]),
+    "tjb_forward_small_workspace_bytes": (ctypes.c_size_t, [_c_int, _c_int, _c_int, _c_int]),
+    "tjb_forward_small": (_c_int, [_p, _c_int, _p, _p, _c_f32, _p, _p, _p, _c_int, _c_int,
+                                   _c_int, _c_int, _c_int, _c_int, _c_int, _p, ctypes.c_size_t,
+                                   _p]),
 }
+
+
+class SmallLayer(ctypes.Structure):
+    """tjb_small_layer: one block's device pointers for tjb_forward_small."""
+
+    _fields_ = [("wqkv", _p), ("wo", _p), ("w1", _p), ("w2", _p), ("bqkv", _p), ("bo", _p),
+                ("b1", _p), ("b2", _p), ("ln1_w", _p), ("ln1_b", _p), ("ln2_w", _p),
+                ("ln2_b", _p), ("ln1_eps", _c_f32), ("ln2_eps", _c_f32)]
 
 _lock = threading.Lock()
 _lib = None

@@ -124,6 +124,10 @@ class Engine:
         # of the smaller shapes still point at them, so they live until those
         # graphs are released.
         self._ln_ws_retired: List[torch.Tensor] = []
+        # Whole-forward kernel (plan.whole_forward): its block pointer table
+        # and one workspace per (batch, seq, device).
+        self._small: Optional[K.SmallModel] = None
+        self._small_ws: Dict[Tuple[int, int, torch.device], torch.Tensor] = {}
         # Pinned host word that every forward ends by copying the device
         # status word into (stream-ordered, no host synchronisation; part of
         # the captured graph too).  The next call reads it: non-zero means a
@@ -181,6 +185,7 @@ class Engine:
         self._gemm_ws = K.gemm_workspace(self.device)
         self._status_host = torch.zeros(1, dtype=torch.int32).pin_memory()
         self._built_for = key
+        self._small = None
         self._graphs.clear()
         self._ln_ws_retired.clear()
 
@@ -240,6 +245,12 @@ class Engine:
             tp_group, _, tp_world = self._tp
             heads //= tp_world
 
+        if (plan.whole_forward and not tp_on and self.head_dim == hd
+                and abs(self.scale - hd ** -0.5) < 1e-12
+                and K.forward_small_supports(batch, seq, d, heads, self.layers[0].w1.shape[0],
+                                             len(self.layers), hd, plan.compute_dtype)):
+            return self._forward_whole(x, mask)
+
         mask_u8 = lengths = flags = tiles = None
         if mask is not None:
             mask_u8 = mask.contiguous().view(torch.uint8) if mask.dtype == torch.bool \
@@ -296,6 +307,24 @@ class Engine:
         _, out = K.fused_add_layernorm(res, pending, fw, fb, feps, out_dtype=self.dtype,
                                        write_residual=False, row_mask=mask_u8)
         return out.view(batch, seq, d)
+
+    def _forward_whole(self, x: torch.Tensor, mask: Optional[torch.Tensor]) -> torch.Tensor:
+        """The whole forward as one launch (tjb_forward_small)."""
+        batch, seq, d = x.shape
+        valid = None
+        if mask is not None:
+            valid = mask.contiguous().view(torch.uint8) if mask.dtype == torch.bool \
+                else (mask != 0).to(torch.uint8)
+        xf = x if (x.dtype == torch.float32 and x.is_contiguous()) else x.float().contiguous()
+        ffn = self.layers[0].w1.shape[0]
+        if self._small is None:
+            self._small = K.SmallModel(self.layers, self.final_ln)
+        key = (batch, seq, x.device)
+        ws = self._small_ws.get(key)
+        if ws is None:
+            ws = self._small_ws[key] = K.forward_small_workspace(batch, seq, d, ffn, x.device)
+        out = K.forward_small(self._small, xf, valid, self.num_heads, ffn, self.causal, ws)
+        return out if out.dtype == self.dtype else out.to(self.dtype)
 
     def _forward_fused_ln(self, x, res, own_res, tiles, lengths, mask_u8, flags, heads, hd,
                           ws) -> torch.Tensor:
@@ -402,7 +431,8 @@ class Engine:
         with torch.cuda.device(self.device):
             torch.cuda.synchronize(self.device)
             status = K.device_status(clear=True) or int(self._status_host[0])
-            for ws in (self._gemm_ws, self._ln_ws, self._attn_sched, *self._ln_ws_retired):
+            for ws in (self._gemm_ws, self._ln_ws, self._attn_sched, *self._ln_ws_retired,
+                       *self._small_ws.values()):
                 if ws is not None:
                     ws.zero_()
             torch.cuda.synchronize(self.device)

@@ -16,6 +16,8 @@ calls capture into CUDA graphs); the library itself never allocates.
 
 from __future__ import annotations
 
+import ctypes
+
 from typing import Optional, Tuple
 
 import torch
@@ -349,6 +351,83 @@ def device_status_async(dst: torch.Tensor, device: torch.device) -> None:
     _lib.check(status, "tjb_device_status_async")
 
 
+# Contract of tjb_forward_small (include/tjb200.h).
+SMALL_MAX_TOKENS, SMALL_MAX_SEQ, SMALL_MAX_LAYERS = 256, 128, 12
+
+
+def forward_small_supports(batch: int, seq: int, d_model: int, heads: int, ffn_dim: int,
+                           layers: int, head_dim: int, dtype: torch.dtype) -> bool:
+    """Whether tjb_forward_small takes this shape (host check, no device work)."""
+    return (dtype == torch.float16 and head_dim == 64 and heads * 64 == d_model
+            and batch * seq <= SMALL_MAX_TOKENS and seq <= SMALL_MAX_SEQ
+            and 0 < layers <= SMALL_MAX_LAYERS and d_model % 128 == 0 and ffn_dim % 128 == 0
+            and d_model <= 1280)
+
+
+def forward_small_workspace(batch: int, seq: int, d_model: int, ffn_dim: int,
+                            device: torch.device) -> torch.Tensor:
+    """A zeroed workspace for :func:`forward_small` (its first words hold the
+    grid barrier; keep one per stream of calls)."""
+    n = int(_lib.lib().tjb_forward_small_workspace_bytes(batch, seq, d_model, ffn_dim))
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+class SmallModel:
+    """The per-block device pointers tjb_forward_small reads (a ctypes array
+    of tjb_small_layer), built once from fp16 weights; keeps the tensors it
+    points to alive."""
+
+    def __init__(self, layers, final_ln) -> None:
+        self._keep = []
+        arr = (_lib.SmallLayer * len(layers))()
+        for i, lw in enumerate(layers):
+            for t in (lw.wqkv, lw.wo, lw.w1, lw.w2):
+                if t.dtype != torch.float16 or not t.is_contiguous():
+                    raise TypeError("tjb_forward_small takes contiguous fp16 weights")
+            fields = dict(wqkv=lw.wqkv, wo=lw.wo, w1=lw.w1, w2=lw.w2, bqkv=lw.bqkv, bo=lw.bo,
+                          b1=lw.b1, b2=lw.b2, ln1_w=lw.ln1_w, ln1_b=lw.ln1_b, ln2_w=lw.ln2_w,
+                          ln2_b=lw.ln2_b)
+            for name, t in fields.items():
+                self._keep.append(t)
+                setattr(arr[i], name, t.data_ptr())
+            arr[i].ln1_eps = float(lw.ln1_eps)
+            arr[i].ln2_eps = float(lw.ln2_eps)
+        self.layers = arr
+        self.count = len(layers)
+        # Bytes of parameters one forward streams, and GEMM weights (for FLOP counts).
+        self.param_bytes = sum(t.numel() * t.element_size() for t in self._keep)
+        self.gemm_params = sum(lw.wqkv.numel() + lw.wo.numel() + lw.w1.numel() + lw.w2.numel()
+                               for lw in layers)
+        self.lnf_w, self.lnf_b, self.lnf_eps = final_ln
+        self._keep += [self.lnf_w, self.lnf_b]
+        self.param_bytes += 2 * self.lnf_w.numel() * 4
+
+
+def forward_small(model: SmallModel, x: torch.Tensor, valid: Optional[torch.Tensor], heads: int,
+                  ffn_dim: int, causal: bool, workspace: torch.Tensor,
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The whole encoder forward in one launch (tjb_forward_small): ``x`` fp32
+    ``[B, S, d]``; ``valid`` uint8 ``[B, S]`` (0 = padded token) or None.
+    Returns fp32 ``[B, S, d]`` with padded rows zero."""
+    _need_cuda(x, valid, workspace)
+    b, s, d = x.shape
+    if x.dtype != torch.float32 or not x.is_contiguous():
+        raise TypeError("x must be contiguous fp32")
+    if valid is not None:
+        if valid.dtype == torch.bool:
+            valid = valid.contiguous().view(torch.uint8)
+        if valid.shape != (b, s) or not valid.is_contiguous():
+            raise ValueError("valid must be a contiguous [B, S] mask")
+    if out is None:
+        out = torch.empty_like(x)
+    status = _lib.lib().tjb_forward_small(
+        ctypes.addressof(model.layers), model.count, _ptr(model.lnf_w), _ptr(model.lnf_b),
+        float(model.lnf_eps), _ptr(x), _ptr(out), _ptr(valid), b, s, d, heads, ffn_dim,
+        int(causal), _lib.TJB_F16, _ptr(workspace), workspace.numel(), _stream(x.device))
+    _lib.check(status, "tjb_forward_small")
+    return out
+
+
 __all__ = [
     "ACT_NONE", "ACT_GELU", "fused_add_layernorm", "layernorm", "gemm_bias", "gemm_workspace",
     "gemm_add_layernorm_workspace", "gemm_add_layernorm_workspace_bytes",
@@ -358,4 +437,5 @@ __all__ = [
     "flash_attention", "flash_supports", "mask_lengths", "mask_lengths_tiles", "row_tiles",
     "device_status",
     "device_status_async",
+    "forward_small", "forward_small_supports", "forward_small_workspace", "SmallModel",
 ]

@@ -80,6 +80,12 @@ class Plan:
     # With fuse_layernorm: also fuse the FFN-out GEMM (False keeps it on the
     # plain GEMM, with stream-K, and a standalone add+LayerNorm after it).
     fuse_layernorm_ffn: bool = True
+    # Run the whole forward as one persistent cooperative kernel
+    # (tjb_forward_small: at most 256 tokens, sequences of at most 128,
+    # head_dim 64, fp16) instead of a launch per op: phases separated by grid
+    # barriers, weight-streaming GEMMs with the weights on the MMA's M side
+    # and split-K for the narrow ones.
+    whole_forward: bool = False
     label: str = "default"
 
     def to_json(self) -> Dict[str, object]:
@@ -94,6 +100,7 @@ class Plan:
             "gemm_stream_k": self.gemm_stream_k,
             "fuse_layernorm": self.fuse_layernorm,
             "fuse_layernorm_ffn": self.fuse_layernorm_ffn,
+            "whole_forward": self.whole_forward,
             "label": self.label,
         }
 
@@ -185,6 +192,8 @@ def select_plan(batch: int, seq: int, d_model: int, heads: int, ffn_dim: int, la
         plan = replace(plan, fuse_layernorm=os.environ["TJ_FUSE_LN"] == "1")
     if os.environ.get("TJ_FUSE_LN_FFN") in ("0", "1"):
         plan = replace(plan, fuse_layernorm_ffn=os.environ["TJ_FUSE_LN_FFN"] == "1")
+    if os.environ.get("TJ_WHOLE_FORWARD") in ("0", "1"):
+        plan = replace(plan, whole_forward=os.environ["TJ_WHOLE_FORWARD"] == "1")
     forced = os.environ.get("TJ_DELTA_DTYPE")
     if forced in _DTYPES:
         plan = replace(plan, delta_dtype=_DTYPES[forced])
