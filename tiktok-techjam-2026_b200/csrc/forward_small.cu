@@ -43,7 +43,7 @@ constexpr int kFsMaxTokens = 256;
 constexpr int kFsMaxSeq = 128;    // attention keeps a sequence's K and V in shared memory
 constexpr int kFsHead = 64;
 constexpr int kFsStages = 4;
-constexpr int kFsQRows = 32;      // query rows per attention unit
+constexpr int kFsQRows = 16;      // query rows per attention unit (two per warp)
 
 struct FsLayer {
   const float* ln1_w;
@@ -78,6 +78,7 @@ struct FsArgs {
   float* part;              // [split][T][d] split-K partials
   unsigned* bar;            // [2]: arrivals, generation (the generation never resets)
   int B, S, T, Tpad, d, H, F, L;
+  int Tsub, n_tsub;         // tokens per GEMM unit (<= 128) and sub-blocks of Tpad
   int causal, bf16;
   int ks_o, ks_2;           // k-splits of the out-projection and FFN-out
   uint32_t idesc;
@@ -103,8 +104,11 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 }
 
 // Grid-wide barrier number `k` (1, 2, ...) of this launch; gen0 is the
-// generation word read at entry.  Bounded: false once the wait exceeds
-// kWaitTimeoutNs (the status word records it) or another CTA gave up.
+// generation word read at entry.  Arrival is a release atomic on the
+// counter (the CTA's writes, gathered by the __syncthreads before it); the
+// last CTA in resets the counter and publishes the generation with a
+// release store, which the others poll with acquire loads.  Bounded: false
+// once the wait exceeds kWaitTimeoutNs (the status word records it).
 __device__ __forceinline__ bool fs_grid_sync(unsigned* bar, unsigned gen0, unsigned k,
                                              volatile int* abort_flag) {
   // Generic-proxy writes of this phase (global activations, and the
@@ -114,28 +118,45 @@ __device__ __forceinline__ bool fs_grid_sync(unsigned* bar, unsigned gen0, unsig
   fence_proxy_async_smem();
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
     const unsigned target = gen0 + k;
-    if (atomicAdd(&bar[0], 1u) == gridDim.x - 1) {
-      atomicExch(&bar[0], 0u);
-      __threadfence();
-      atomicExch(&bar[1], target);
+    unsigned old;
+    asm volatile("atom.add.release.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(bar) : "memory");
+    if (old == gridDim.x - 1) {
+      asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(bar) : "memory");
+      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(bar + 1), "r"(target) : "memory");
     } else {
       const uint64_t t0 = globaltimer();
-      while (static_cast<int>(fs_ld_acquire_u32(&bar[1]) - target) < 0) {
-        if (globaltimer() - t0 > kWaitTimeoutNs) {
+      for (uint32_t i = 1; static_cast<int>(fs_ld_acquire_u32(bar + 1) - target) < 0; ++i) {
+        if ((i & 255) == 0 && globaltimer() - t0 > kWaitTimeoutNs) {
           record_status(TJB_ERR_DEVICE_TIMEOUT);
           *abort_flag = 1;
           break;
         }
-        __nanosleep(32);
       }
     }
-    __threadfence();
   }
   __syncthreads();
   fence_proxy_async_global();
   return *abort_flag == 0;
+}
+
+// L2 prefetch of the weight boxes this CTA's units of a coming GEMM phase
+// will load (one thread; the boxes are those fs_gemm's producer issues).
+__device__ __forceinline__ void fs_prefetch_weights(const FsArgs& a, const CUtensorMap* tmW,
+                                                    int N, int K, int ks) {
+  const int kb_total = K / 64;
+  const int kbu = (kb_total + ks - 1) / ks;
+  const int units = (N / 128) * ks * a.n_tsub;
+  for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    if (u % a.n_tsub != 0) continue;  // the other token blocks read the same boxes
+    const int rest = u / a.n_tsub;
+    const int nt = rest / ks, kc = rest - (rest / ks) * ks;
+    for (int kb = kc * kbu; kb < min(kb_total, kc * kbu + kbu); ++kb)
+      asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                       reinterpret_cast<uint64_t>(tmW)),
+                   "r"(kb * 64), "r"(nt * 128)
+                   : "memory");
+  }
 }
 
 // Ring and accumulator positions; every role keeps its own copy and moves
@@ -170,20 +191,23 @@ __device__ __forceinline__ void fs_gemm(const FsArgs& a, const CUtensorMap* tmW,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kb_total = K / 64;
   const int kbu = (kb_total + ks - 1) / ks;
-  const int units = (N / 128) * ks;
-  auto unit_range = [&](int u, int& nt, int& kc, int& kb0, int& kb1) {
-    nt = u / ks;
-    kc = u - nt * ks;
+  const int units = (N / 128) * ks * a.n_tsub;
+  // Unit u: token sub-block u % n_tsub, then k-split, then feature tile.
+  auto unit_range = [&](int u, int& nt, int& kc, int& kb0, int& kb1, int& ts) {
+    ts = u % a.n_tsub;
+    const int rest = u / a.n_tsub;
+    nt = rest / ks;
+    kc = rest - nt * ks;
     kb0 = kc * kbu;
     kb1 = min(kb_total, kb0 + kbu);
   };
   if (warp == 0) {
     if (lane == 0) {
-      const uint32_t tx = FsSmem::kABytes + static_cast<uint32_t>(a.Tpad) * 128u;
+      const uint32_t tx = FsSmem::kABytes + static_cast<uint32_t>(a.Tsub) * 128u;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
-        int nt, kc, kb0, kb1;
-        unit_range(u, nt, kc, kb0, kb1);
+        int nt, kc, kb0, kb1, ts;
+        unit_range(u, nt, kc, kb0, kb1, ts);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&sh.empty[ring.stage], ring.phase ^ 1, sh.abort_flag)) {
             ok = false;
@@ -192,7 +216,8 @@ __device__ __forceinline__ void fs_gemm(const FsArgs& a, const CUtensorMap* tmW,
           mbar_arrive_expect_tx(&sh.full[ring.stage], tx);
           tma_load_2d(sh.sA + ring.stage * FsSmem::kABytes, tmW, &sh.full[ring.stage], kb * 64,
                       nt * 128);
-          tma_load_2d(sh.sB + ring.stage * FsSmem::kBBytes, tmX, &sh.full[ring.stage], kb * 64, 0);
+          tma_load_2d(sh.sB + ring.stage * FsSmem::kBBytes, tmX, &sh.full[ring.stage], kb * 64,
+                      ts * a.Tsub);
           ring.issued |= 1u << ring.stage;
           ring.last_parity = (ring.last_parity & ~(1u << ring.stage)) | (ring.phase << ring.stage);
           if (++ring.stage == kFsStages) {
@@ -208,8 +233,8 @@ __device__ __forceinline__ void fs_gemm(const FsArgs& a, const CUtensorMap* tmW,
     };
     bool ok = true;
     for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
-      int nt, kc, kb0, kb1;
-      unit_range(u, nt, kc, kb0, kb1);
+      int nt, kc, kb0, kb1, ts;
+      unit_range(u, nt, kc, kb0, kb1, ts);
       if (kb0 >= kb1) continue;
       if (!wait(&sh.tempty[ring.acc], ring.acc_phase ^ 1)) break;
       tc_fence_after();
@@ -243,8 +268,8 @@ __device__ __forceinline__ void fs_gemm(const FsArgs& a, const CUtensorMap* tmW,
     const int quad = warp & 3;         // TMEM lanes (features) this warp may read
     const int half = (warp - 2) >> 2;  // which token chunks
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
-      int nt, kc, kb0, kb1;
-      unit_range(u, nt, kc, kb0, kb1);
+      int nt, kc, kb0, kb1, ts;
+      unit_range(u, nt, kc, kb0, kb1, ts);
       if (kb0 >= kb1) continue;
       if (!__all_sync(0xffffffffu, mbar_wait(&sh.tfull[ring.acc], ring.acc_phase, sh.abort_flag)))
         break;
@@ -253,15 +278,16 @@ __device__ __forceinline__ void fs_gemm(const FsArgs& a, const CUtensorMap* tmW,
       const uint32_t taddr = sh.tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(ring.acc * kFsMaxTokens);
       const float bn = ks == 1 && bias != nullptr ? __ldg(bias + n) : 0.f;
+      const int t0 = ts * a.Tsub;
 #pragma unroll 1
-      for (int c = half; c * 32 < a.T; c += 2) {
+      for (int c = half; c * 32 < a.Tsub && t0 + c * 32 < a.T; c += 2) {
         uint32_t r[32];
         tmem_ld32(taddr + c * 32, r);
         tmem_ld_wait(r);
         if (ks == 1) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const int t = c * 32 + i;
+            const int t = t0 + c * 32 + i;
             float v = __uint_as_float(r[i]) + bn;
             if (act) v = gelu_erf(v);
             if (t < a.T) out16[static_cast<int64_t>(t) * N + n] = __half_as_ushort(__float2half_rn(v));
@@ -270,7 +296,7 @@ __device__ __forceinline__ void fs_gemm(const FsArgs& a, const CUtensorMap* tmW,
           float* dst = part + static_cast<int64_t>(kc) * a.T * N + n;
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const int t = c * 32 + i;
+            const int t = t0 + c * 32 + i;
             if (t < a.T) __stcg(dst + static_cast<int64_t>(t) * N, __uint_as_float(r[i]));
           }
         }
@@ -286,21 +312,21 @@ __device__ __forceinline__ void fs_gemm(const FsArgs& a, const CUtensorMap* tmW,
   }
 }
 
-// Attention, fp32 on the CUDA cores: a unit is (sequence b, head hh, 32
-// query rows); K and V rows [0, keys) of the head go to shared memory (K
-// padded to 65 floats a row, so lane j's key j reads conflict-free), eight
-// warps take four query rows each: lane j scores keys j, j + 32, ... (keys
-// after the row when causal, and padded keys, are left out), the row's max
-// and sum meet by shuffles, and lane j accumulates output dimensions 2j and
-// 2j + 1.  A row with no key left is written as zero.
+// Attention, fp32 on the CUDA cores: a unit is (sequence b, head hh, 16
+// query rows).  K rows [0, keys) of the head go to shared memory
+// dimension-major (sKT[e][j]) so that lane l reads keys 4l .. 4l + 3 of one
+// dimension with a single 16-byte load; V stays row-major (lane l reads
+// dimensions 2l, 2l + 1).  Eight warps take two query rows each and share
+// every K and V load between them.  Keys after a row (causal) and padded
+// keys are left out; a row with no key left is written as zero.
 __device__ __forceinline__ void fs_attention(const FsArgs& a, float* sm) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qb = (a.S + kFsQRows - 1) / kFsQRows;
   const int units = a.B * a.H * n_qb;
   const int ld = 3 * a.d;  // qkv row length
-  float* sK = sm;                          // [kFsMaxSeq][65]
-  float* sV = sK + kFsMaxSeq * 65;         // [kFsMaxSeq][64]
-  float* sQ = sV + kFsMaxSeq * kFsHead;    // [32][64]
+  float* sKT = sm;                           // [kFsHead][kFsMaxSeq]
+  float* sV = sKT + kFsHead * kFsMaxSeq;     // [kFsMaxSeq][kFsHead]
+  float* sQ = sV + kFsMaxSeq * kFsHead;      // [kFsQRows][kFsHead]
   for (int u = blockIdx.x; u < units; u += gridDim.x) {
     const int qb = u % n_qb;
     const int bh = u / n_qb;
@@ -308,75 +334,113 @@ __device__ __forceinline__ void fs_attention(const FsArgs& a, float* sm) {
     const int q0 = qb * kFsQRows, q1 = min(a.S, q0 + kFsQRows);
     const int keys = a.causal ? q1 : a.S;
     const uint8_t* vk = a.valid != nullptr ? a.valid + static_cast<int64_t>(b) * a.S : nullptr;
-    const uint16_t* base = a.qkv + static_cast<int64_t>(b) * a.S * ld;
+    const uint16_t* base = a.qkv + static_cast<int64_t>(b) * a.S * ld + hh * kFsHead;
     __syncthreads();  // the previous unit is done with the shared tiles
+    // K: consecutive threads take consecutive keys of one dimension pair.
+    for (int idx = threadIdx.x; idx < keys * 32; idx += kFsThreads) {
+      const int r = idx % keys, c2 = (idx / keys) * 2;
+      const __half2 k2 =
+          *reinterpret_cast<const __half2*>(base + static_cast<int64_t>(r) * ld + a.d + c2);
+      sKT[c2 * kFsMaxSeq + r] = __low2float(k2);
+      sKT[(c2 + 1) * kFsMaxSeq + r] = __high2float(k2);
+    }
     for (int idx = threadIdx.x; idx < keys * 32; idx += kFsThreads) {
       const int r = idx >> 5, c2 = (idx & 31) * 2;
-      const uint16_t* row = base + static_cast<int64_t>(r) * ld + hh * kFsHead + c2;
-      const __half2 k2 = *reinterpret_cast<const __half2*>(row + a.d);
-      const __half2 v2 = *reinterpret_cast<const __half2*>(row + 2 * a.d);
-      sK[r * 65 + c2] = __low2float(k2);
-      sK[r * 65 + c2 + 1] = __high2float(k2);
-      sV[r * kFsHead + c2] = __low2float(v2);
-      sV[r * kFsHead + c2 + 1] = __high2float(v2);
+      const float2 v = __half22float2(*reinterpret_cast<const __half2*>(
+          base + static_cast<int64_t>(r) * ld + 2 * a.d + c2));
+      *reinterpret_cast<float2*>(sV + r * kFsHead + c2) = v;
     }
     for (int idx = threadIdx.x; idx < (q1 - q0) * 32; idx += kFsThreads) {
       const int r = idx >> 5, c2 = (idx & 31) * 2;
-      const __half2 q2 = *reinterpret_cast<const __half2*>(
-          base + static_cast<int64_t>(q0 + r) * ld + hh * kFsHead + c2);
-      sQ[r * kFsHead + c2] = __low2float(q2);
-      sQ[r * kFsHead + c2 + 1] = __high2float(q2);
+      const float2 q = __half22float2(
+          *reinterpret_cast<const __half2*>(base + static_cast<int64_t>(q0 + r) * ld + c2));
+      *reinterpret_cast<float2*>(sQ + r * kFsHead + c2) = q;
     }
     __syncthreads();
-    if (warp >= 8) continue;
-    for (int rr = 0; rr < kFsQRows / 8; ++rr) {
-      const int i = q0 + warp * (kFsQRows / 8) + rr;
-      if (i >= q1) break;
-      const int lim = a.causal ? i + 1 : a.S;  // keys [0, lim), less the padded ones
-      uint32_t* dst = reinterpret_cast<uint32_t*>(
-          a.ctx + (static_cast<int64_t>(b) * a.S + i) * a.d + hh * kFsHead + 2 * lane);
-      const float* q = sQ + (i - q0) * kFsHead;
-      float s[kFsMaxSeq / 32];
-      float mx = -INFINITY;
+    if (warp >= kFsQRows / 2) continue;
+    const int iA = q0 + 2 * warp, iB = iA + 1;
+    if (iA >= q1) continue;
+    const bool hasB = iB < q1;
+    const int limA = a.causal ? iA + 1 : a.S;
+    const int limB = hasB ? (a.causal ? iB + 1 : a.S) : 0;
+    const float* qA = sQ + (iA - q0) * kFsHead;
+    const float* qB = sQ + (hasB ? iB - q0 : iA - q0) * kFsHead;
+    float sA[4] = {0.f, 0.f, 0.f, 0.f}, sB[4] = {0.f, 0.f, 0.f, 0.f};
+    if (4 * lane < keys) {
+#pragma unroll 4
+      for (int e4 = 0; e4 < kFsHead / 4; ++e4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(qA + 4 * e4);
+        const float4 b4 = *reinterpret_cast<const float4*>(qB + 4 * e4);
+        const float qa[4] = {a4.x, a4.y, a4.z, a4.w}, qbv[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
-      for (int m = 0; m < kFsMaxSeq / 32; ++m) {
-        const int j = lane + 32 * m;
-        s[m] = -INFINITY;
-        if (j < lim && (vk == nullptr || vk[j] != 0)) {
-          const float* k = sK + j * 65;
-          float dot = 0.f;
-#pragma unroll 16
-          for (int e = 0; e < kFsHead; ++e) dot = fmaf(q[e], k[e], dot);
-          s[m] = dot;
-          mx = fmaxf(mx, dot);
+        for (int ee = 0; ee < 4; ++ee) {
+          const float4 k4 =
+              *reinterpret_cast<const float4*>(sKT + (4 * e4 + ee) * kFsMaxSeq + 4 * lane);
+          sA[0] = fmaf(qa[ee], k4.x, sA[0]);
+          sA[1] = fmaf(qa[ee], k4.y, sA[1]);
+          sA[2] = fmaf(qa[ee], k4.z, sA[2]);
+          sA[3] = fmaf(qa[ee], k4.w, sA[3]);
+          sB[0] = fmaf(qbv[ee], k4.x, sB[0]);
+          sB[1] = fmaf(qbv[ee], k4.y, sB[1]);
+          sB[2] = fmaf(qbv[ee], k4.z, sB[2]);
+          sB[3] = fmaf(qbv[ee], k4.w, sB[3]);
         }
       }
+    }
+    float mA = -INFINITY, mB = -INFINITY;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      float sum = 0.f;
+    for (int m = 0; m < 4; ++m) {
+      const int j = 4 * lane + m;
+      const bool live = j < keys && (vk == nullptr || vk[j] != 0);
+      sA[m] = live && j < limA ? sA[m] : -INFINITY;
+      sB[m] = live && j < limB ? sB[m] : -INFINITY;
+      mA = fmaxf(mA, sA[m]);
+      mB = fmaxf(mB, sB[m]);
+    }
 #pragma unroll
-      for (int m = 0; m < kFsMaxSeq / 32; ++m) {
-        s[m] = s[m] != -INFINITY ? exp2f((s[m] - mx) * a.scale_log2) : 0.f;
-        sum += s[m];
-      }
+    for (int o = 16; o > 0; o >>= 1) {
+      mA = fmaxf(mA, __shfl_xor_sync(0xffffffffu, mA, o));
+      mB = fmaxf(mB, __shfl_xor_sync(0xffffffffu, mB, o));
+    }
+    float lA = 0.f, lB = 0.f;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      float o0 = 0.f, o1 = 0.f;
+    for (int m = 0; m < 4; ++m) {
+      sA[m] = sA[m] != -INFINITY ? exp2f((sA[m] - mA) * a.scale_log2) : 0.f;
+      sB[m] = sB[m] != -INFINITY ? exp2f((sB[m] - mB) * a.scale_log2) : 0.f;
+      lA += sA[m];
+      lB += sB[m];
+    }
 #pragma unroll
-      for (int m = 0; m < kFsMaxSeq / 32; ++m) {
-        if (32 * m >= lim) break;
-        for (int jj = 0; jj < 32; ++jj) {
-          const int j = 32 * m + jj;
-          const float p = __shfl_sync(0xffffffffu, s[m], jj);
-          if (j < lim) {
-            o0 = fmaf(p, sV[j * kFsHead + 2 * lane], o0);
-            o1 = fmaf(p, sV[j * kFsHead + 2 * lane + 1], o1);
-          }
+    for (int o = 16; o > 0; o >>= 1) {
+      lA += __shfl_xor_sync(0xffffffffu, lA, o);
+      lB += __shfl_xor_sync(0xffffffffu, lB, o);
+    }
+    float2 oA = make_float2(0.f, 0.f), oB = make_float2(0.f, 0.f);
+    const int jmax = max(limA, limB) < keys ? max(limA, limB) : keys;
+    for (int src = 0; 4 * src < jmax; ++src) {
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const float pa = __shfl_sync(0xffffffffu, sA[m], src);
+        const float pb = __shfl_sync(0xffffffffu, sB[m], src);
+        const int j = 4 * src + m;
+        if (j < jmax) {
+          const float2 v = *reinterpret_cast<const float2*>(sV + j * kFsHead + 2 * lane);
+          oA.x = fmaf(pa, v.x, oA.x);
+          oA.y = fmaf(pa, v.y, oA.y);
+          oB.x = fmaf(pb, v.x, oB.x);
+          oB.y = fmaf(pb, v.y, oB.y);
         }
       }
-      const float inv = sum > 0.f ? 1.f / sum : 0.f;
-      const __half2 r2 = __floats2half2_rn(o0 * inv, o1 * inv);
-      *dst = *reinterpret_cast<const uint32_t*>(&r2);
+    }
+    const float iaA = lA > 0.f ? 1.f / lA : 0.f;
+    const __half2 rA = __floats2half2_rn(oA.x * iaA, oA.y * iaA);
+    *reinterpret_cast<__half2*>(a.ctx + (static_cast<int64_t>(b) * a.S + iA) * a.d +
+                                hh * kFsHead + 2 * lane) = rA;
+    if (hasB) {
+      const float iaB = lB > 0.f ? 1.f / lB : 0.f;
+      const __half2 rB = __floats2half2_rn(oB.x * iaB, oB.y * iaB);
+      *reinterpret_cast<__half2*>(a.ctx + (static_cast<int64_t>(b) * a.S + iB) * a.d +
+                                  hh * kFsHead + 2 * lane) = rB;
     }
   }
 }
@@ -408,21 +472,43 @@ __device__ __forceinline__ void fs_layernorm(const FsArgs& a, const float* in, c
   const int d = a.d;
   const float inv_d = 1.f / static_cast<float>(d);
   for (int t = blockIdx.x; t < a.T; t += gridDim.x) {
-    float v[4];
+    // v = in (+ partials in order, + bias) for this thread's columns; the
+    // partials of all four columns are loaded in one sweep (two chains per
+    // column), so their latencies overlap.
+    float v[4], v2[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int j = threadIdx.x + kFsThreads * c;
+      v[c] = j < d ? in[static_cast<int64_t>(t) * d + j] : 0.f;
+      v2[c] = 0.f;
+    }
+    if (part != nullptr) {
+      const int64_t stride = static_cast<int64_t>(a.T) * d;
+      const float* pp = part + static_cast<int64_t>(t) * d + threadIdx.x;
+      int kc = 0;
+      for (; kc + 2 <= ks; kc += 2) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          if (threadIdx.x + kFsThreads * c < d) {
+            v[c] += __ldcg(pp + kc * stride + kFsThreads * c);
+            v2[c] += __ldcg(pp + (kc + 1) * stride + kFsThreads * c);
+          }
+        }
+      }
+      if (kc < ks) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (threadIdx.x + kFsThreads * c < d) v[c] += __ldcg(pp + kc * stride + kFsThreads * c);
+      }
+    }
     float s = 0.f;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       const int j = threadIdx.x + kFsThreads * c;
-      v[c] = 0.f;
       if (j < d) {
-        float x = in[static_cast<int64_t>(t) * d + j];
-        if (part != nullptr) {
-          for (int kc = 0; kc < ks; ++kc)
-            x += __ldcg(part + (static_cast<int64_t>(kc) * a.T + t) * d + j);
-          x += __ldg(bias + j);
-        }
-        v[c] = x;
-        s += x;
+        v[c] += v2[c];
+        if (part != nullptr) v[c] += __ldg(bias + j);
+        s += v[c];
       }
     }
     const float mean = fs_block_sum(s, red) * inv_d;
@@ -500,6 +586,7 @@ __global__ void __launch_bounds__(kFsThreads, 1) forward_small_kernel(const __gr
 
   for (int l = 0; l < a.L; ++l) {
     const FsLayer& ly = a.layer[l];
+    if (threadIdx.x == 0) fs_prefetch_weights(a, &a.w_qkv[l], 3 * d, d, 1);
     if (l == 0)
       fs_layernorm(a, a.x, nullptr, 0, nullptr, a.res, a.h, nullptr, ly.ln1_w, ly.ln1_b,
                    ly.ln1_eps, red);
@@ -509,13 +596,16 @@ __global__ void __launch_bounds__(kFsThreads, 1) forward_small_kernel(const __gr
     if (!fs_grid_sync(a.bar, gen0, ++k, sh.abort_flag)) goto done;
     fs_gemm(a, &a.w_qkv[l], &a.x_h, 3 * d, d, 1, ly.bqkv, 0, a.qkv, nullptr, sh, ring);
     if (!fs_grid_sync(a.bar, gen0, ++k, sh.abort_flag)) goto done;
+    if (threadIdx.x == 0) fs_prefetch_weights(a, &a.w_o[l], d, d, a.ks_o);
     fs_attention(a, sm);
     if (!fs_grid_sync(a.bar, gen0, ++k, sh.abort_flag)) goto done;
     fs_gemm(a, &a.w_o[l], &a.x_ctx, d, d, a.ks_o, nullptr, 0, nullptr, a.part, sh, ring);
     if (!fs_grid_sync(a.bar, gen0, ++k, sh.abort_flag)) goto done;
+    if (threadIdx.x == 0) fs_prefetch_weights(a, &a.w_1[l], a.F, d, 1);
     fs_layernorm(a, a.res, a.part, a.ks_o, ly.bo, a.res, a.h2, nullptr, ly.ln2_w, ly.ln2_b,
                  ly.ln2_eps, red);
     if (!fs_grid_sync(a.bar, gen0, ++k, sh.abort_flag)) goto done;
+    if (threadIdx.x == 0) fs_prefetch_weights(a, &a.w_2[l], d, a.F, a.ks_2);
     fs_gemm(a, &a.w_1[l], &a.x_h2, a.F, d, 1, ly.b1, 1, a.hidden, nullptr, sh, ring);
     if (!fs_grid_sync(a.bar, gen0, ++k, sh.abort_flag)) goto done;
     fs_gemm(a, &a.w_2[l], &a.x_hidden, d, a.F, a.ks_2, nullptr, 0, nullptr, a.part, sh, ring);
@@ -568,8 +658,10 @@ int fs_split(int N, int K, int grid) {
 
 FsLayout fs_layout(int T, int d, int F, int grid) {
   FsLayout L;
-  L.ks_o = fs_split(d, d, grid);
-  L.ks_2 = fs_split(d, F, grid);
+  const int Tpad = (T + 15) / 16 * 16;
+  const int n_tsub = (Tpad + 127) / 128;  // token sub-blocks of a GEMM phase
+  L.ks_o = fs_split(d, d, std::max(1, grid / n_tsub));
+  L.ks_2 = fs_split(d, F, std::max(1, grid / n_tsub));
   size_t at = 0;
   auto take = [&](size_t bytes) {
     const size_t here = at;
@@ -641,6 +733,7 @@ extern "C" int tjb_forward_small(const tjb_small_layer* layers, int L, const flo
   memset(&a, 0, sizeof(a));
   a.H = H;
   const int Tpad = (T + 15) / 16 * 16;
+  const int Tsub = Tpad < 128 ? Tpad : 128;  // tokens per GEMM unit
   auto wmap = [&](CUtensorMap* m, const void* w, int rows, int K) {
     const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(rows)};
     const uint64_t strides[1] = {static_cast<uint64_t>(K) * 2};
@@ -650,7 +743,7 @@ extern "C" int tjb_forward_small(const tjb_small_layer* layers, int L, const flo
   auto xmap = [&](CUtensorMap* m, const void* p, int K) {
     const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(T)};
     const uint64_t strides[1] = {static_cast<uint64_t>(K) * 2};
-    const uint32_t box[2] = {64, static_cast<uint32_t>(Tpad)};
+    const uint32_t box[2] = {64, static_cast<uint32_t>(Tsub)};
     return make_tmap_16bit(m, 2, p, dims, strides, box, false);
   };
   for (int l = 0; l < L; ++l) {
@@ -696,13 +789,15 @@ extern "C" int tjb_forward_small(const tjb_small_layer* layers, int L, const flo
   a.T = T;
   a.d = d;
   a.Tpad = Tpad;
+  a.Tsub = Tsub;
+  a.n_tsub = (Tpad + Tsub - 1) / Tsub;
   a.F = F;
   a.L = L;
   a.causal = causal;
   a.bf16 = 0;
   a.ks_o = lay.ks_o;
   a.ks_2 = lay.ks_2;
-  a.idesc = idesc_f16(128, Tpad, false, false);
+  a.idesc = idesc_f16(128, Tsub, false, false);
   a.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(kFsHead));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
