@@ -312,6 +312,13 @@ __device__ __forceinline__ void fs_gemm(const FsArgs& a, const CUtensorMap* tmW,
   }
 }
 
+// Two 16-bit values written earlier in this launch by another CTA: an L2
+// (coherent) load, never the read-only path.
+__device__ __forceinline__ __half2 fs_ld_half2(const uint16_t* p) {
+  const unsigned u = __ldcg(reinterpret_cast<const unsigned*>(p));
+  return *reinterpret_cast<const __half2*>(&u);
+}
+
 // Attention, fp32 on the CUDA cores: a unit is (sequence b, head hh, 16
 // query rows).  K rows [0, keys) of the head go to shared memory
 // dimension-major (sKT[e][j]) so that lane l reads keys 4l .. 4l + 3 of one
@@ -336,25 +343,50 @@ __device__ __forceinline__ void fs_attention(const FsArgs& a, float* sm) {
     const uint8_t* vk = a.valid != nullptr ? a.valid + static_cast<int64_t>(b) * a.S : nullptr;
     const uint16_t* base = a.qkv + static_cast<int64_t>(b) * a.S * ld + hh * kFsHead;
     __syncthreads();  // the previous unit is done with the shared tiles
-    // K: consecutive threads take consecutive keys of one dimension pair.
-    for (int idx = threadIdx.x; idx < keys * 32; idx += kFsThreads) {
-      const int r = idx % keys, c2 = (idx / keys) * 2;
-      const __half2 k2 =
-          *reinterpret_cast<const __half2*>(base + static_cast<int64_t>(r) * ld + a.d + c2);
-      sKT[c2 * kFsMaxSeq + r] = __low2float(k2);
-      sKT[(c2 + 1) * kFsMaxSeq + r] = __high2float(k2);
+    // Eight loads per thread in flight before their shared-memory stores.
+    // K: consecutive threads take consecutive keys of one dimension pair
+    // (dimension-major stores); V and Q: consecutive threads take
+    // consecutive dimension pairs of a row.
+    const int nk = keys * 32, nq = (q1 - q0) * 32;
+    for (int i0 = 0; i0 < nk; i0 += 8 * kFsThreads) {
+      __half2 kv[8], vv[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int idx = i0 + i * kFsThreads + threadIdx.x;
+        if (idx < nk) {
+          const int r = idx % keys, c2 = (idx / keys) * 2;
+          kv[i] = fs_ld_half2(base + static_cast<int64_t>(r) * ld + a.d + c2);
+          const int rv = idx >> 5, cv = (idx & 31) * 2;
+          vv[i] = fs_ld_half2(base + static_cast<int64_t>(rv) * ld + 2 * a.d + cv);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int idx = i0 + i * kFsThreads + threadIdx.x;
+        if (idx < nk) {
+          const int r = idx % keys, c2 = (idx / keys) * 2;
+          sKT[c2 * kFsMaxSeq + r] = __low2float(kv[i]);
+          sKT[(c2 + 1) * kFsMaxSeq + r] = __high2float(kv[i]);
+          const int rv = idx >> 5, cv = (idx & 31) * 2;
+          *reinterpret_cast<float2*>(sV + rv * kFsHead + cv) = __half22float2(vv[i]);
+        }
+      }
     }
-    for (int idx = threadIdx.x; idx < keys * 32; idx += kFsThreads) {
-      const int r = idx >> 5, c2 = (idx & 31) * 2;
-      const float2 v = __half22float2(*reinterpret_cast<const __half2*>(
-          base + static_cast<int64_t>(r) * ld + 2 * a.d + c2));
-      *reinterpret_cast<float2*>(sV + r * kFsHead + c2) = v;
-    }
-    for (int idx = threadIdx.x; idx < (q1 - q0) * 32; idx += kFsThreads) {
-      const int r = idx >> 5, c2 = (idx & 31) * 2;
-      const float2 q = __half22float2(
-          *reinterpret_cast<const __half2*>(base + static_cast<int64_t>(q0 + r) * ld + c2));
-      *reinterpret_cast<float2*>(sQ + r * kFsHead + c2) = q;
+    for (int i0 = 0; i0 < nq; i0 += 2 * kFsThreads) {
+      __half2 qv[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int idx = i0 + i * kFsThreads + threadIdx.x;
+        if (idx < nq)
+          qv[i] = fs_ld_half2(base + static_cast<int64_t>(q0 + (idx >> 5)) * ld + (idx & 31) * 2);
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int idx = i0 + i * kFsThreads + threadIdx.x;
+        if (idx < nq)
+          *reinterpret_cast<float2*>(sQ + (idx >> 5) * kFsHead + (idx & 31) * 2) =
+              __half22float2(qv[i]);
+      }
     }
     __syncthreads();
     if (warp >= kFsQRows / 2) continue;
