@@ -102,11 +102,11 @@ FLUSH_BYTES = 256 << 20
 # dram__bytes_read.sum + dram__bytes_write.sum over those launches / their
 # number, from one ncu capture of this bench's own command (a one-pass
 # metric set on the full workload).  None where no capture was taken.
-# Config 2: 12 launches, QKV and FFN1 on CTA pairs (17.7-18.0 and 20.4-20.9
-# MB), FFN2 on the single-CTA stream-K kernel (63.3-69.6 MB); the outputs
-# mostly stay in the 126 MB L2 during a launch, so the figure sits below the
-# algorithmic bytes (A + W read, C written).
-GEMM_TRAFFIC_PER_LAUNCH = {2: 34.84e6}
+# Config 2: 12 launches, all on CTA pairs: QKV and FFN1 (17.7-18.1 and
+# 20.1-20.8 MB), FFN2 with stream-K over the pairs (64.4-68.4 MB); the
+# outputs mostly stay in the 126 MB L2 during a launch, so the figure sits
+# below the algorithmic bytes (A + W read, C written).
+GEMM_TRAFFIC_PER_LAUNCH = {2: 34.73e6}
 
 
 def use_package() -> None:
