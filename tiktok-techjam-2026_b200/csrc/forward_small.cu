@@ -40,6 +40,7 @@ namespace {
 constexpr int kFsThreads = 320;   // producer warp, MMA warp, eight epilogue warps
 constexpr int kFsMaxLayers = 12;
 constexpr int kFsMaxTokens = 256;
+constexpr int kFsUnitTokens = 128; // tokens of one GEMM unit (the MMA's N): a TMEM accumulator
 constexpr int kFsMaxSeq = 128;    // attention keeps a sequence's K and V in shared memory
 constexpr int kFsHead = 64;
 constexpr int kFsStages = 4;
@@ -79,7 +80,7 @@ struct FsArgs {
   unsigned* bar;            // [2]: arrivals, generation (the generation never resets)
   int B, S, T, Tpad, d, H, F, L;
   int Tsub, n_tsub;         // tokens per GEMM unit (<= 128) and sub-blocks of Tpad
-  int causal, bf16;
+  int causal;
   int ks_o, ks_2;           // k-splits of the out-projection and FFN-out
   uint32_t idesc;
   float scale_log2;         // softmax scale * log2(e)
@@ -87,11 +88,14 @@ struct FsArgs {
 
 struct FsSmem {
   static constexpr uint32_t kABytes = 128 * 64 * 2;
-  static constexpr uint32_t kBBytes = kFsMaxTokens * 64 * 2;
+  static constexpr uint32_t kBBytes = kFsUnitTokens * 64 * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr size_t kRing = static_cast<size_t>(kFsStages) * kStageBytes;
   static constexpr size_t kBytes = 1024 + kRing + 1024;
 };
+// The attention phase keeps K, V and a query block in the (then idle) ring.
+static_assert((2 * kFsHead * kFsMaxSeq + kFsQRows * kFsHead) * sizeof(float) <= FsSmem::kRing,
+              "attention tiles must fit the operand ring");
 
 __device__ __forceinline__ unsigned fs_ld_acquire_u32(const unsigned* p) {
   unsigned v;
@@ -238,7 +242,7 @@ __device__ __forceinline__ void fs_gemm(const FsArgs& a, const CUtensorMap* tmW,
       if (kb0 >= kb1) continue;
       if (!wait(&sh.tempty[ring.acc], ring.acc_phase ^ 1)) break;
       tc_fence_after();
-      const uint32_t d_tmem = sh.tmem_base + static_cast<uint32_t>(ring.acc * kFsMaxTokens);
+      const uint32_t d_tmem = sh.tmem_base + static_cast<uint32_t>(ring.acc * kFsUnitTokens);
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!wait(&sh.full[ring.stage], ring.phase)) {
           ok = false;
@@ -276,7 +280,7 @@ __device__ __forceinline__ void fs_gemm(const FsArgs& a, const CUtensorMap* tmW,
       tc_fence_after();
       const int n = nt * 128 + quad * 32 + lane;  // this thread's output feature
       const uint32_t taddr = sh.tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                             static_cast<uint32_t>(ring.acc * kFsMaxTokens);
+                             static_cast<uint32_t>(ring.acc * kFsUnitTokens);
       const float bn = ks == 1 && bias != nullptr ? __ldg(bias + n) : 0.f;
       const int t0 = ts * a.Tsub;
 #pragma unroll 1
@@ -603,7 +607,7 @@ __global__ void __launch_bounds__(kFsThreads, 1) forward_small_kernel(const __gr
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 2 * kFsMaxTokens);
+    tmem_alloc(tmem_slot, 2 * kFsUnitTokens);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -662,7 +666,7 @@ done:
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(sh.tmem_base, 2 * kFsMaxTokens);
+    tmem_dealloc(sh.tmem_base, 2 * kFsUnitTokens);
   }
 }
 
@@ -768,7 +772,7 @@ extern "C" int tjb_forward_small(const tjb_small_layer* layers, int L, const flo
   memset(&a, 0, sizeof(a));
   a.H = H;
   const int Tpad = (T + 15) / 16 * 16;
-  const int Tsub = Tpad < 128 ? Tpad : 128;  // tokens per GEMM unit
+  const int Tsub = Tpad < kFsUnitTokens ? Tpad : kFsUnitTokens;  // tokens per GEMM unit
   auto wmap = [&](CUtensorMap* m, const void* w, int rows, int K) {
     const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(rows)};
     const uint64_t strides[1] = {static_cast<uint64_t>(K) * 2};
@@ -829,7 +833,6 @@ extern "C" int tjb_forward_small(const tjb_small_layer* layers, int L, const flo
   a.F = F;
   a.L = L;
   a.causal = causal;
-  a.bf16 = 0;
   a.ks_o = lay.ks_o;
   a.ks_2 = lay.ks_2;
   a.idesc = idesc_f16(128, Tsub, false, false);
