@@ -17,7 +17,7 @@
 //   then       final LayerNorm (+ the last partials), padded rows written as 0
 //
 // GEMMs are swapped so that the weights fill the MMA's M side: a work unit
-// is 128 output features x all (padded) tokens x a range of k-blocks;
+// is 128 output features x up to 128 (padded) tokens x a range of k-blocks;
 // warp 0 TMA-loads the weight tile (128 x 64) and the activation tile
 // (tokens x 64, both K-major, 128-byte swizzle) into a 4-stage ring, warp 1
 // issues tcgen05.mma (M=128, N=tokens, K=16) into one of two TMEM
@@ -25,9 +25,11 @@
 // tokens per load) and store 32 consecutive features of a token per warp
 // instruction.  The out-projection and FFN-out have few output features
 // (d / 128 tiles), so their k-blocks are split over the grid and the next
-// LayerNorm phase adds the partials in a fixed order.  Attention (a sequence
-// of at most 128 tokens) runs on the CUDA cores in fp32, a CTA per (sequence,
-// head, 32 query rows).  Activations stay in L2 between phases.
+// LayerNorm phase adds the partials in a fixed order.  While a phase runs,
+// each CTA prefetches into L2 the weight boxes of its next GEMM phase.
+// Attention (a sequence of at most 128 tokens) runs on the CUDA cores in
+// fp32, a CTA per (sequence, head, 16 query rows).  Activations stay in L2
+// between phases.
 #include <algorithm>
 #include <cstring>
 #include <mutex>
