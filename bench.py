@@ -68,6 +68,7 @@ import json
 import os
 import statistics
 import sys
+import types
 import threading
 import time
 from datetime import timedelta
@@ -610,7 +611,8 @@ def kernel_main(argv) -> int:
     import tjkernels.kernels as K
 
     ap = argparse.ArgumentParser(prog="bench.py --kernel")
-    ap.add_argument("kernel", choices=["gemm", "attn", "ln", "ffn", "ffn_single", "gemm_ln"])
+    ap.add_argument("kernel", choices=["gemm", "attn", "ln", "ffn", "ffn_single", "gemm_ln",
+                                       "small"])
     ap.add_argument("dims", type=int, nargs="+")
     ap.add_argument("--act", choices=["none", "gelu"], default="none")
     ap.add_argument("--out", choices=["f16", "f32"], default="f16")
@@ -672,6 +674,24 @@ def kernel_main(argv) -> int:
         fn = lambda: K.gemm_add_layernorm(a, w, bias, res, gamma, beta, 1e-5,
                                           residual_out=res, out=out, workspace=ws)
         flops = 2.0 * m * n * k
+    elif args.kernel == "small":
+        # The whole forward in one launch (tjb_forward_small): dims B S d H F L,
+        # default-like random weights, all tokens valid, causal.
+        b, s, d, h, f, layers = args.dims
+        one = lambda n: torch.ones(n, device=dev)
+        zero = lambda n: torch.zeros(n, device=dev)
+        blocks = [types.SimpleNamespace(
+            wqkv=randn(3 * d, d, scale=d ** -0.5), wo=randn(d, d, scale=d ** -0.5),
+            w1=randn(f, d, scale=d ** -0.5), w2=randn(d, f, scale=f ** -0.5),
+            bqkv=zero(3 * d), bo=zero(d), b1=zero(f), b2=zero(d), ln1_w=one(d), ln1_b=zero(d),
+            ln2_w=one(d), ln2_b=zero(d), ln1_eps=1e-5, ln2_eps=1e-5) for _ in range(layers)]
+        small = K.SmallModel(blocks, (one(d), zero(d), 1e-5))
+        x = torch.randn(b, s, d, device=dev, generator=g)
+        ws = K.forward_small_workspace(b, s, d, f, dev)
+        out = torch.empty_like(x)
+        fn = lambda: K.forward_small(small, x, None, h, f, True, ws, out=out)
+        flops = 2.0 * b * s * small.gemm_params + layers * 4.0 * d * b * s * (s + 1) / 2
+        nbytes = float(small.param_bytes + 2 * x.numel() * 4)
     else:
         # ffn: the two GEMM launches through a hidden scratch; ffn_single: the
         # one-kernel form whose hidden activations stay on chip.
