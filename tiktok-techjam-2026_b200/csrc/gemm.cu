@@ -313,6 +313,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tmem_relinquish();
   }
+  // The weights are never written by the kernels this launch overlaps:
+  // pull the first k-blocks of this CTA's first B tile into L2 while the
+  // previous kernel drains (its tile as the full M would place it).
+  if (warp == 0 && lane == 0) {
+    int m_blk, n_blk;
+    tile_coords(static_cast<int>(blockIdx.x), (args.M + kBM - 1) / kBM, (args.N + BN - 1) / BN,
+                m_blk, n_blk);
+    for (int kb = 0; kb < Cfg::kStages && kb * kBK < args.K; ++kb)
+      tma_prefetch_2d(&tmB, kb * kBK, n_blk * BN);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -601,6 +611,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_relinquish_pair();
   }
   tc_fence_before();
+  // This CTA's half of the first B tile, first k-blocks, into L2 before the
+  // wait (weights are never written by the kernels this launch overlaps).
+  if (warp == 0 && lane == 0) {
+    int mp, n_blk;
+    tile_coords(static_cast<int>(blockIdx.x >> 1), ((args.M + kBM - 1) / kBM + 1) / 2,
+                (args.N + BN - 1) / BN, mp, n_blk);
+    for (int kb = 0; kb < kStages && kb * kBK < args.K; ++kb)
+      tma_prefetch_2d(&tmB, kb * kBK, n_blk * BN + static_cast<int>(rank) * 128);
+  }
   // Both CTAs' barriers are initialised and their tensor memory allocated
   // before either signals the other.
   cluster_sync();

@@ -117,6 +117,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
+  // The first k-blocks of this CTA's first W tile into L2 before the wait
+  // (weights are never written by the kernels this launch overlaps).
+  if (warp == 0 && lane == 0)
+    for (int kb = 0; kb < kLnStages && kb * kBK < args.K; ++kb)
+      tma_prefetch_2d(&tmB, kb * kBK, (static_cast<int>(blockIdx.x) % C) * 256);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
