@@ -352,7 +352,8 @@ typedef struct {
   float ln2_eps;
 } tjb_small_layer;
 
-/* Workspace bytes tjb_forward_small needs for B sequences of S tokens. */
+/* Workspace bytes tjb_forward_small needs for B sequences of S tokens on
+ * the current device (the split-K partials scale with its SM count). */
 size_t tjb_forward_small_workspace_bytes(int B, int S, int d, int F);
 
 /*

@@ -82,6 +82,40 @@ def test_gemm_add_layernorm_contract_without_device():
     assert call(a=fake + 4) == 3                               # misaligned operand
 
 
+def test_forward_small_contract_without_device():
+    """The whole-forward entry point rejects bad arguments, unsupported
+    dtypes and shapes outside its contract before it touches a device, and
+    sizes its workspace on the host."""
+    import ctypes
+    from tjkernels import _lib
+    lib = _lib.lib()
+    assert lib.tjb_forward_small_workspace_bytes(0, 64, 768, 3072) == 0
+    small = lib.tjb_forward_small_workspace_bytes(1, 64, 768, 3072)
+    assert small > 0 and lib.tjb_forward_small_workspace_bytes(4, 64, 768, 3072) > small
+    fake = 1 << 20
+    layers = (_lib.SmallLayer * 4)()
+    for ly in layers:
+        for name, _ in _lib.SmallLayer._fields_[:12]:
+            setattr(ly, name, fake)
+    f16, bf16 = _lib.TJB_F16, _lib.TJB_BF16
+
+    def call(b=1, s=64, d=768, h=12, f=3072, n_layers=4, dtype=f16, ws=fake, lys=layers):
+        return lib.tjb_forward_small(ctypes.addressof(lys) if lys is not None else None,
+                                     n_layers, fake, fake, 1e-5, fake, fake, None, b, s, d, h, f,
+                                     1, dtype, ws, 1 << 30, None)
+
+    assert call(lys=None) == 1                     # no layer table
+    assert call(ws=None) == 1                      # no workspace
+    assert call(n_layers=0) == 1
+    assert call(dtype=bf16) == 4                   # fp16 only
+    assert call(d=768, h=6) == 2                   # head_dim 128
+    assert call(b=3, s=100, d=512, h=8, f=2048) == 2   # 300 tokens
+    assert call(b=1, s=200, d=512, h=8, f=2048) == 2   # sequence longer than 128
+    assert call(f=3000) == 2                       # F not a multiple of 128
+    assert call(n_layers=13) == 2                  # more than 12 blocks
+    assert call() == 8                             # valid call, no device here
+
+
 def test_ffn_noalloc_limit_without_device():
     """The allocation-free FFN refuses T * F beyond its fixed array before it
     touches a device or a pointer (so the pointers here are never used)."""
