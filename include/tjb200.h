@@ -198,12 +198,18 @@ int tjb_flash_fwd(const void* qkv, void* out, int B, int S, int H, int hd,
  * call; the kernel leaves them zero again when it completes, so one pair
  * serves any number of calls that run one after another (same stream, or a
  * CUDA graph).  Calls that may run at the same time need separate pairs.
+ * skip_dead_rows: 0 writes the rows of query tiles wholly at or past
+ * lengths[b] as 0, as tjb_flash_fwd does; non-zero (prefix masks only)
+ * leaves those rows unspecified (work items with no live query tile are
+ * dropped unwritten; others still write 0) -- for callers
+ * that, like the forward with a live-tile list, never let a padded row reach
+ * a valid one and zero padded rows at the end.
  * No counterpart in the reference (its Triton grid is static).
  */
 int tjb_flash_fwd_sched(const void* qkv, void* out, int B, int S, int H, int hd,
                         float scale, int causal, const int32_t* lengths,
                         const uint8_t* key_mask, const int32_t* mask_flags,
-                        int dtype, int32_t* sched, tjb_stream_t stream);
+                        int dtype, int32_t* sched, int skip_dead_rows, tjb_stream_t stream);
 
 /*
  * Feed-forward block out = gelu_erf(h * w1^T + b1) * w2^T + b2.

@@ -419,6 +419,46 @@ def test_flash_dynamic_schedule_matches_static(hd, mask_kind):
         assert sched.tolist() == [0, 0]
 
 
+@pytest.mark.parametrize("hd", [64, 128])
+@pytest.mark.parametrize("mask_kind", ["prefix", "general"])
+def test_flash_skip_dead_rows(hd, mask_kind):
+    """skip_dead_rows leaves the rows of query tiles wholly past a prefix
+    length as they were and gives the same bits everywhere else; with a mask
+    that is not a prefix nothing is skipped and every row matches."""
+    b, s, h = 5, 900, 4
+    g = torch.Generator(device=DEV).manual_seed(7 * hd + len(mask_kind))
+    qkv = torch.randn(b, s, 3, h, hd, device=DEV, generator=g).half()
+    if mask_kind == "prefix":
+        lengths = torch.tensor([900, 1, 300, 0, 641], dtype=torch.int32, device=DEV)
+        mask = torch.arange(s, device=DEV)[None, :] < lengths[:, None]
+    else:
+        mask = torch.rand(b, s, device=DEV, generator=g) > 0.4
+        mask[:, 0] = True
+    lens, flags = K().mask_lengths(mask)
+    kw = dict(lengths=lens, key_mask=mask.to(torch.uint8), mask_flags=flags)
+    ref = K().flash_attention(qkv, h, causal=True, **kw)
+    sched = torch.zeros(2, dtype=torch.int32, device=DEV)
+    # Fill the caching allocator's next block with a marker so that unwritten
+    # rows are visible: flash_attention's output reuses the freed block.
+    marker = torch.full((b * s, h * hd), 7.0, dtype=torch.float16, device=DEV)
+    del marker
+    out = K().flash_attention(qkv, h, causal=True, sched=sched, skip_dead_rows=True, **kw)
+    assert sched.tolist() == [0, 0]
+    live = torch.ones(b, s, dtype=torch.bool, device=DEV)
+    if mask_kind == "prefix":
+        tile0 = (torch.arange(s, device=DEV) // 128 * 128)[None, :]
+        live = tile0 < lens.long()[:, None]
+    live = live.reshape(-1)
+    assert torch.equal(out[live], ref[live])
+    if mask_kind == "prefix":
+        # Dead rows are unspecified: left as they were (7.0) where the whole
+        # work item was skipped, zero where a live tile shares the item.
+        dead = out[~live]
+        unwritten = (dead == 7.0).all(dim=1)
+        assert bool((unwritten | (dead == 0).all(dim=1)).all())
+        assert int(unwritten.sum()) > 0, "no dead work item was skipped"
+
+
 def test_flash_unsupported_head_dim():
     from tjkernels._lib import KernelError
     qkv = torch.randn(1, 64, 3, 4, 32, device=DEV).bfloat16()

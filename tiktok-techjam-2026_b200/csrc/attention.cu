@@ -48,6 +48,7 @@ struct AttnArgs {
   float scale_log2;
   int causal;
   int bf16;
+  int skip_dead;  // prefix mask: items with no key to attend are not queued (rows unwritten)
   uint32_t idesc_qk, idesc_pv;
 };
 
@@ -255,14 +256,26 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     if (lane == 0) {
       // -------------------------------------------------------------- producer
       uint32_t seq = 0, n_items = 0;  // K/V tiles issued, items started
+      uint32_t claims = 0;            // items claimed, queued or not
       bool ok = true;
       for (uint32_t qn = 0;; ++qn) {
         // Claim the next work item (from the shared counter, heaviest causal
         // rows first, or a fixed stride without one) and queue it for the
         // MMA and softmax warps; -1 ends their loops.
         int w = args.sched != nullptr ? atomicAdd(args.sched, 1)
-                                      : static_cast<int>(blockIdx.x + qn * gridDim.x);
+                                      : static_cast<int>(blockIdx.x + (claims++) * gridDim.x);
         if (w >= total || !ok) w = -1;
+        PairItem it;
+        if (w >= 0) {
+          it = decode_pair(w, args, num_pairs, prefix);
+          // With skip_dead, an item with nothing to attend (both query tiles
+          // wholly past a prefix length) is dropped here and its rows are
+          // left unwritten; the same queue slot takes the next claim.
+          if (args.skip_dead && prefix && max(it.n_kv[0], it.n_kv[1]) == 0) {
+            --qn;
+            continue;
+          }
+        }
         const uint32_t islot = qn % kItemSlots;
         if (qn >= kItemSlots &&
             !mbar_wait(&item_empty[islot], (qn / kItemSlots - 1) & 1, abort_flag))
@@ -270,7 +283,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         item_q[islot] = w;
         mbar_arrive(&item_full[islot]);
         if (w < 0) break;
-        const PairItem it = decode_pair(w, args, num_pairs, prefix);
         const int n = max(it.n_kv[0], it.n_kv[1]);
         if (n == 0) continue;
         const uint32_t slot = n_items % kQSlots;
@@ -630,7 +642,7 @@ namespace tjb {
 namespace {
 int flash_fwd(const void* qkv, void* out, int B, int S, int H, int hd, float scale, int causal,
               const int32_t* lengths, const uint8_t* key_mask, const int32_t* mask_flags,
-              int dtype, int32_t* sched, tjb_stream_t stream) {
+              int dtype, int32_t* sched, int skip_dead, tjb_stream_t stream) {
   if (!qkv || !out || B <= 0 || S <= 0 || H <= 0 || hd <= 0) return TJB_ERR_INVALID_ARGUMENT;
   if (dtype != TJB_F16 && dtype != TJB_BF16) return TJB_ERR_UNSUPPORTED_DTYPE;
   if (hd != 64 && hd != 128) return TJB_ERR_BAD_SHAPE;
@@ -652,6 +664,7 @@ int flash_fwd(const void* qkv, void* out, int B, int S, int H, int hd, float sca
   a.scale_log2 = scale * 1.4426950408889634f;
   a.causal = causal != 0;
   a.bf16 = dtype == TJB_BF16;
+  a.skip_dead = skip_dead != 0;
   a.idesc_qk = idesc_f16(kTileQ, kTileK, a.bf16 != 0, false);
   a.idesc_pv = idesc_f16(kTileQ, hd, a.bf16 != 0, true);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -664,14 +677,14 @@ extern "C" int tjb_flash_fwd(const void* qkv, void* out, int B, int S, int H, in
                              int causal, const int32_t* lengths, const uint8_t* key_mask,
                              const int32_t* mask_flags, int dtype, tjb_stream_t stream) {
   return tjb::flash_fwd(qkv, out, B, S, H, hd, scale, causal, lengths, key_mask, mask_flags,
-                        dtype, nullptr, stream);
+                        dtype, nullptr, 0, stream);
 }
 
 extern "C" int tjb_flash_fwd_sched(const void* qkv, void* out, int B, int S, int H, int hd,
                                    float scale, int causal, const int32_t* lengths,
                                    const uint8_t* key_mask, const int32_t* mask_flags, int dtype,
-                                   int32_t* sched, tjb_stream_t stream) {
+                                   int32_t* sched, int skip_dead_rows, tjb_stream_t stream) {
   if (sched == nullptr) return TJB_ERR_INVALID_ARGUMENT;
   return tjb::flash_fwd(qkv, out, B, S, H, hd, scale, causal, lengths, key_mask, mask_flags,
-                        dtype, sched, stream);
+                        dtype, sched, skip_dead_rows, stream);
 }

@@ -34,7 +34,7 @@ SIGNATURES = {
     "tjb_flash_fwd": (_c_int, [_p, _p, _c_int, _c_int, _c_int, _c_int, _c_f32, _c_int,
                                _p, _p, _p, _c_int, _p]),
     "tjb_flash_fwd_sched": (_c_int, [_p, _p, _c_int, _c_int, _c_int, _c_int, _c_f32, _c_int,
-                                     _p, _p, _p, _c_int, _p, _p]),
+                                     _p, _p, _p, _c_int, _p, _c_int, _p]),
     "tjb_ffn": (_c_int, [_p, _p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int,
                          _c_int, _p]),
     "tjb_ffn_tiles": (_c_int, [_p, _p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int,

@@ -284,7 +284,8 @@ class Engine:
             ctx = K.flash_attention(qkv.view(batch, seq, 3, heads, hd), heads,
                                     causal=self.causal, lengths=lengths, key_mask=mask_u8,
                                     mask_flags=flags, scale=self.scale,
-                                    sched=self._attn_sched if plan.attn_dynamic else None)
+                                    sched=self._attn_sched if plan.attn_dynamic else None,
+                                    skip_dead_rows=tiles is not None)
             attn_out = K.gemm_bias(ctx, lw.wo, lw.bo, out_dtype=delta_dtype, m_tiles=tiles,
                                    workspace=ws)
             if tp_on:
@@ -354,7 +355,8 @@ class Engine:
             ctx = K.flash_attention(qkv.view(batch, seq, 3, heads, hd), heads,
                                     causal=self.causal, lengths=lengths, key_mask=mask_u8,
                                     mask_flags=flags, scale=self.scale,
-                                    sched=self._attn_sched if plan.attn_dynamic else None)
+                                    sched=self._attn_sched if plan.attn_dynamic else None,
+                                    skip_dead_rows=tiles is not None)
             # The first write goes to a fresh buffer unless the residual is
             # already private (it may be the caller's input).
             res, h2 = K.gemm_add_layernorm(ctx, lw.wo, lw.bo, res, lw.ln2_w, lw.ln2_b,

@@ -258,12 +258,16 @@ def flash_attention(qkv: torch.Tensor, heads: int, causal: bool = True,
                     key_mask: Optional[torch.Tensor] = None,
                     mask_flags: Optional[torch.Tensor] = None,
                     scale: Optional[float] = None,
-                    sched: Optional[torch.Tensor] = None) -> torch.Tensor:
+                    sched: Optional[torch.Tensor] = None,
+                    skip_dead_rows: bool = False) -> torch.Tensor:
     """qkv ``[B, S, 3, H, hd]`` (contiguous) -> out ``[B*S, H*hd]``.
 
     ``sched``: optional int32 ``[2]`` device tensor, zero, that switches to
     the dynamic work queue (``tjb_flash_fwd_sched``); the kernel leaves it
     zero again.  Calls that may overlap on the GPU need separate tensors.
+    ``skip_dead_rows`` (with ``sched`` and a prefix mask): query tiles wholly
+    past ``lengths[b]`` are not computed and their rows are left unwritten
+    instead of zeroed.
     """
     _need_cuda(qkv, lengths, key_mask, mask_flags, sched)
     b, s, three, h, hd = qkv.shape
@@ -279,7 +283,7 @@ def flash_attention(qkv: torch.Tensor, heads: int, causal: bool = True,
         status = _lib.lib().tjb_flash_fwd_sched(
             _ptr(qkv), _ptr(out), b, s, h, hd, float(scale), int(causal), _ptr(lengths),
             _ptr(key_mask), _ptr(mask_flags), _code(qkv.dtype), _ptr(sched),
-            _stream(qkv.device))
+            int(skip_dead_rows), _stream(qkv.device))
         _lib.check(status, "tjb_flash_fwd_sched")
         return out
     status = _lib.lib().tjb_flash_fwd(
