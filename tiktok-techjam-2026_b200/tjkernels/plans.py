@@ -70,12 +70,13 @@ class Plan:
     # Run the out-projection and FFN-out GEMMs with the residual add and the
     # next LayerNorm in their epilogue (tjb_gemm_add_layernorm; d_model 256,
     # 512, 768 or 1024), so their outputs never reach HBM and those
-    # LayerNorms need no pass of their own.  Off by default; on in the tuned
-    # plan of the B4 S4096 shape (1-3 % faster there) and, for the
-    # out-projection only, of the B8 S1024 shape (0.7 %; fusing its FFN-out
-    # too is 4 % slower, since that GEMM needs stream-K for its K = 4096
-    # tail wave); slower where the GEMM has too few 128 x 256 tiles (B1 S64:
-    # one row block, three CTAs).
+    # LayerNorms need no pass of their own.  Off by default; on, for the
+    # out-projection only, in the tuned plan of the B8 S1024 shape (0.7 %;
+    # fusing its FFN-out too is 4 % slower, since that GEMM needs stream-K
+    # for its K = 4096 tail wave).  The B4 S4096 plan keeps its LayerNorms
+    # standalone: with CTA-pair GEMMs and the persistent LayerNorm kernel the
+    # fused form no longer wins there.  Slower where the GEMM has too few
+    # 128 x 256 tiles (B1 S64: one row block, three CTAs).
     fuse_layernorm: bool = False
     # With fuse_layernorm: also fuse the FFN-out GEMM (False keeps it on the
     # plain GEMM, with stream-K, and a standalone add+LayerNorm after it).
