@@ -646,7 +646,8 @@ def kernel_main(argv) -> int:
             mask = torch.arange(s, device=dev)[None, :] < lengths[:, None]
             lens, flags = K.mask_lengths(mask)
             kw = dict(lengths=lens, key_mask=mask.to(torch.uint8), mask_flags=flags,
-                      sched=torch.zeros(2, dtype=torch.int32, device=dev))
+                      sched=torch.zeros(2, dtype=torch.int32, device=dev),
+                      skip_dead_rows=True)
             n_list = lengths.tolist()
         else:
             n_list = [s] * b
