@@ -518,6 +518,103 @@ def e2e_leg(fwd, x_cpu, mask_cpu, steps, dev, stream, flush, barrier):
     return e_start.elapsed_time(e_end) / steps
 
 
+class PeerBuffers:
+    """GPU 0's scatter/gather buffers mapped into every rank (CUDA IPC), so
+    that each rank's copy engine pulls its input shard from GPU 0 and pushes
+    its output shard back over NVLink with plain cudaMemcpyAsync calls: no
+    SM of GPU 0 is taken from its own forward, as an NCCL scatter/gather
+    kernel would.  Rank 0 owns one cudaMalloc block for the inputs of every
+    rank and one for `depth` sets of outputs; the others open their handles
+    in their own device's context (peer access over NVLink).  `ok` is False
+    on every rank when any rank failed to set up (the caller then uses
+    NCCL); every rank takes the same collective steps either way."""
+
+    def __init__(self, dist, rank, world, dev, shard_bytes, depth, inputs):
+        self.rank, self.world, self.shard, self.depth = rank, world, shard_bytes, depth
+        self.ok = False
+        self.x_base = self.o_base = None
+        self._owned = []
+        self._opened = []
+        try:
+            from cuda.bindings import runtime as rt
+        except Exception:
+            rt = None
+        self.rt = rt
+        handles = [None, None]
+        # BENCH_SG_NCCL=1 keeps the NCCL scatter/gather (for comparisons).
+        good = rt is not None and os.environ.get("BENCH_SG_NCCL") != "1"
+        if rank == 0 and good:
+            try:
+                for i, nbytes in enumerate((world * shard_bytes, depth * world * shard_bytes)):
+                    err, ptr = rt.cudaMalloc(nbytes)
+                    good = good and err == rt.cudaError_t.cudaSuccess
+                    if not good:
+                        break
+                    self._owned.append(ptr)
+                    err, h = rt.cudaIpcGetMemHandle(ptr)
+                    good = good and err == rt.cudaError_t.cudaSuccess
+                    handles[i] = bytes(h.reserved) if good else None
+                if good:
+                    self.x_base, self.o_base = self._owned
+                    for r, t in enumerate(inputs):
+                        (err,) = rt.cudaMemcpy(self.x_base + r * shard_bytes, t.data_ptr(),
+                                               shard_bytes,
+                                               rt.cudaMemcpyKind.cudaMemcpyDeviceToDevice)
+                        good = good and err == rt.cudaError_t.cudaSuccess
+            except Exception:
+                good = False
+        box = [handles if good else None]
+        dist.broadcast_object_list(box, src=0, device=dev)
+        if rank != 0:
+            good = rt is not None and box[0] is not None and os.environ.get("BENCH_SG_NCCL") != "1"
+            if good:
+                try:
+                    bases = []
+                    for raw in box[0]:
+                        h = rt.cudaIpcMemHandle_t()
+                        h.reserved = raw
+                        err, ptr = rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess)
+                        good = good and err == rt.cudaError_t.cudaSuccess
+                        if not good:
+                            break
+                        self._opened.append(ptr)
+                        bases.append(ptr)
+                    if good:
+                        self.x_base, self.o_base = bases
+                except Exception:
+                    good = False
+        flag = torch.tensor([1 if good else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        self.ok = bool(flag.item())
+
+    def pull_input(self, dst: torch.Tensor, stream: torch.cuda.Stream) -> None:
+        rt = self.rt
+        (err,) = rt.cudaMemcpyAsync(dst.data_ptr(), self.x_base + self.rank * self.shard,
+                                    self.shard, rt.cudaMemcpyKind.cudaMemcpyDeviceToDevice,
+                                    stream.cuda_stream)
+        if err != rt.cudaError_t.cudaSuccess:
+            raise RuntimeError(f"peer input copy failed: {err}")
+
+    def push_output(self, src: torch.Tensor, k: int, stream: torch.cuda.Stream) -> None:
+        rt = self.rt
+        dst = self.o_base + (k * self.world + self.rank) * self.shard
+        (err,) = rt.cudaMemcpyAsync(dst, src.data_ptr(), self.shard,
+                                    rt.cudaMemcpyKind.cudaMemcpyDeviceToDevice,
+                                    stream.cuda_stream)
+        if err != rt.cudaError_t.cudaSuccess:
+            raise RuntimeError(f"peer output copy failed: {err}")
+
+    def close(self, dist, dev) -> None:
+        """Peers unmap first; rank 0 frees after a barrier."""
+        torch.cuda.synchronize(dev)
+        for ptr in self._opened:
+            self.rt.cudaIpcCloseMemHandle(ptr)
+        dist.barrier(device_ids=[dev.index])
+        for ptr in self._owned:
+            self.rt.cudaFree(ptr)
+        self._opened, self._owned = [], []
+
+
 # -------------------------------------------------------- reference GPU path
 
 def run_reference_gpu(args, rank, world):
@@ -807,6 +904,7 @@ def main():
         # buffer sets: step i+1's scatter and step i's gather overlap the
         # forwards (every rank issues them in the same order).
         sg_ms = 0.0
+        sg_transport = None
         if world > 1 and not tp:
             depth = 2
             x_all = None
@@ -814,6 +912,10 @@ def main():
             if rank == 0:
                 x_all = [synthetic_case(b, s, d, 100000, pad, r, world)[0].to(dev)
                          for r in range(world)]
+            shard_bytes = b * s * d * 4
+            peers = PeerBuffers(dist, rank, world, dev, shard_bytes, depth, x_all or [])
+            sg_transport = "p2p" if peers.ok else "nccl"
+            if not peers.ok and rank == 0:
                 out_all = [[torch.empty((b, s, d), dtype=torch.float32, device=dev)
                             for _ in range(world)] for _ in range(depth)]
             x_sg = [torch.empty_like(x) for _ in range(depth)]
@@ -821,10 +923,22 @@ def main():
             ev_in = [torch.cuda.Event() for _ in range(depth)]
             ev_done = [torch.cuda.Event() for _ in range(depth)]
 
+            def scatter_into(dst):
+                if peers.ok:
+                    peers.pull_input(dst, comm)
+                else:
+                    dist.scatter(dst, x_all, src=0)
+
+            def gather_from(out, k):
+                if peers.ok:
+                    peers.push_output(out, k, comm)
+                else:
+                    dist.gather(out, out_all[k], dst=0)
+
             def sg_steps(n):
                 with torch.cuda.stream(comm):
                     comm.wait_stream(stream)
-                    dist.scatter(x_sg[0], x_all, src=0)
+                    scatter_into(x_sg[0])
                     ev_in[0].record(comm)
                 for i in range(n):
                     k, kn = i % depth, (i + 1) % depth
@@ -832,7 +946,7 @@ def main():
                         with torch.cuda.stream(comm):
                             if i >= 1:
                                 comm.wait_event(ev_done[kn])  # forward i-1 read x_sg[kn]
-                            dist.scatter(x_sg[kn], x_all, src=0)
+                            scatter_into(x_sg[kn])
                             ev_in[kn].record(comm)
                     stream.wait_event(ev_in[k])
                     out = model(x_sg[k], mask)
@@ -840,7 +954,7 @@ def main():
                     flush.zero_()
                     with torch.cuda.stream(comm):
                         comm.wait_event(ev_done[k])
-                        dist.gather(out, out_all[k], dst=0)
+                        gather_from(out, k)
                         out.record_stream(comm)
                 stream.wait_stream(comm)
 
@@ -855,6 +969,7 @@ def main():
             torch.cuda.synchronize(dev)
             barrier()
             sg_ms = sg_start.elapsed_time(sg_end) / args.steps
+            peers.close(dist, dev)
             del x_all, out_all
 
         # -------------------------------- per-kernel timing of the plan (eager)
@@ -971,10 +1086,13 @@ def main():
             line["scatter_gather"] = {
                 "value": tokens / (sg_max / 1e3), "unit": "tokens/s", "ms_per_step": sg_max,
                 "bytes_per_step": 2 * (world - 1) * b * s * d * 4,
-                "note": "inputs start on GPU 0; per step NCCL scatter of the shards and "
-                        "gather of the outputs on a side stream, step i+1's scatter and "
-                        "step i's gather overlapping the forwards (two buffer sets); max "
-                        "over ranks"}
+                "transport": sg_transport,
+                "note": "inputs start on GPU 0; per step every rank pulls its input shard "
+                        "from GPU 0 and pushes its output shard back with copy-engine "
+                        "cudaMemcpyAsync over NVLink through CUDA IPC mappings (transport "
+                        "p2p; NCCL scatter/gather if the mapping is not available), on a "
+                        "side stream, step i+1's scatter and step i's gather overlapping "
+                        "the forwards (two buffer sets); max over ranks"}
         if device_status != 0:
             print(json.dumps(line), flush=True)
             raise SystemExit(f"a kernel recorded device status {device_status} "
