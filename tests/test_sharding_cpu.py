@@ -190,3 +190,37 @@ def test_tp_shard_shapes_and_errors():
     assert torch.equal(w["wqkv"][:16], enc.layers[0].attention.q_proj.weight[16:32])
     with pytest.raises(ValueError):
         tp_shard(enc.layers[0], 0, 3)
+
+
+def _peer_rank_main(rank, world, port, nccl_env, out_path):
+    import sys
+    from pathlib import Path
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    if nccl_env:
+        os.environ["BENCH_SG_NCCL"] = "1"
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+        import bench
+        dev = torch.device("cpu")
+        inputs = [torch.zeros(4) for _ in range(world)] if rank == 0 else []
+        peers = bench.PeerBuffers(dist, rank, world, dev, 16, 2, inputs)
+        # Every rank agrees, and the collectives after it still line up.
+        flag = torch.tensor([1 if peers.ok else 0])
+        dist.all_reduce(flag)
+        torch.save({"ok": peers.ok, "sum": int(flag.item())}, f"{out_path}.{rank}")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("nccl_env", [False, True])
+def test_peer_buffers_fall_back_together(tmp_path, nccl_env):
+    """The copy-engine scatter/gather set-up of bench.py on two gloo ranks
+    without a GPU: it cannot map device memory, so every rank reports the
+    NCCL fallback and all ranks still take the same collective steps."""
+    port = _free_port()
+    out = str(tmp_path / "peer")
+    mp.spawn(_peer_rank_main, args=(2, port, nccl_env, out), nprocs=2, join=True)
+    for r in range(2):
+        got = torch.load(f"{out}.{r}")
+        assert got["ok"] is False and got["sum"] == 0
