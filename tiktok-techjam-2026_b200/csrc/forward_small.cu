@@ -28,7 +28,7 @@
 // LayerNorm phase adds the partials in a fixed order.  While a phase runs,
 // each CTA prefetches into L2 the weight boxes of its next GEMM phase.
 // Attention (a sequence of at most 128 tokens) runs on the CUDA cores in
-// fp32, a CTA per (sequence, head, 16 query rows).  Activations stay in L2
+// fp32, a CTA per (sequence, head, 8 query rows).  Activations stay in L2
 // between phases.
 #include <algorithm>
 #include <cstring>
@@ -46,7 +46,7 @@ constexpr int kFsUnitTokens = 128; // tokens of one GEMM unit (the MMA's N): a T
 constexpr int kFsMaxSeq = 128;    // attention keeps a sequence's K and V in shared memory
 constexpr int kFsHead = 64;
 constexpr int kFsStages = 4;
-constexpr int kFsQRows = 16;      // query rows per attention unit (two per warp)
+constexpr int kFsQRows = 8;       // query rows per attention unit (two per warp)
 
 struct FsLayer {
   const float* ln1_w;
@@ -325,13 +325,15 @@ __device__ __forceinline__ __half2 fs_ld_half2(const uint16_t* p) {
   return *reinterpret_cast<const __half2*>(&u);
 }
 
-// Attention, fp32 on the CUDA cores: a unit is (sequence b, head hh, 16
-// query rows).  K rows [0, keys) of the head go to shared memory
-// dimension-major (sKT[e][j]) so that lane l reads keys 4l .. 4l + 3 of one
-// dimension with a single 16-byte load; V stays row-major (lane l reads
-// dimensions 2l, 2l + 1).  Eight warps take two query rows each and share
-// every K and V load between them.  Keys after a row (causal) and padded
-// keys are left out; a row with no key left is written as zero.
+// Attention, fp32 on the CUDA cores: a unit is (sequence b, head hh,
+// kFsQRows query rows); more, smaller units spread a small batch over more
+// SMs.  K rows [0, keys) of the head go to shared memory dimension-major
+// (sKT[e][j]) so that lane l reads keys 4l .. 4l + 3 of one dimension with
+// a single 16-byte load; V stays row-major (lane l reads dimensions 2l,
+// 2l + 1).  kFsQRows / 2 warps take two query rows each and share every K
+// and V load between them; all warps load the tiles.  Keys after a row
+// (causal) and padded keys are left out; a row with no key left is written
+// as zero.
 __device__ __forceinline__ void fs_attention(const FsArgs& a, float* sm) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qb = (a.S + kFsQRows - 1) / kFsQRows;
