@@ -46,7 +46,7 @@ constexpr int kFsUnitTokens = 128; // tokens of one GEMM unit (the MMA's N): a T
 constexpr int kFsMaxSeq = 128;    // attention keeps a sequence's K and V in shared memory
 constexpr int kFsHead = 64;
 constexpr int kFsStages = 4;
-constexpr int kFsQRows = 8;       // query rows per attention unit (two per warp)
+constexpr int kFsQRows = 16;      // most query rows per attention unit (two per warp)
 
 struct FsLayer {
   const float* ln1_w;
@@ -83,6 +83,7 @@ struct FsArgs {
   int B, S, T, Tpad, d, H, F, L;
   int Tsub, n_tsub;         // tokens per GEMM unit (<= 128) and sub-blocks of Tpad
   int causal;
+  int qrows;                // query rows per attention unit: 8, or 16 when 8 would overfill the grid
   int ks_o, ks_2;           // k-splits of the out-projection and FFN-out
   uint32_t idesc;
   float scale_log2;         // softmax scale * log2(e)
@@ -326,17 +327,17 @@ __device__ __forceinline__ __half2 fs_ld_half2(const uint16_t* p) {
 }
 
 // Attention, fp32 on the CUDA cores: a unit is (sequence b, head hh,
-// kFsQRows query rows); more, smaller units spread a small batch over more
-// SMs.  K rows [0, keys) of the head go to shared memory dimension-major
+// a.qrows query rows); 8-row units spread a small batch over more SMs,
+// 16-row units keep a larger one within one unit per CTA.  K rows [0, keys) of the head go to shared memory dimension-major
 // (sKT[e][j]) so that lane l reads keys 4l .. 4l + 3 of one dimension with
 // a single 16-byte load; V stays row-major (lane l reads dimensions 2l,
-// 2l + 1).  kFsQRows / 2 warps take two query rows each and share every K
+// 2l + 1).  a.qrows / 2 warps take two query rows each and share every K
 // and V load between them; all warps load the tiles.  Keys after a row
 // (causal) and padded keys are left out; a row with no key left is written
 // as zero.
 __device__ __forceinline__ void fs_attention(const FsArgs& a, float* sm) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_qb = (a.S + kFsQRows - 1) / kFsQRows;
+  const int n_qb = (a.S + a.qrows - 1) / a.qrows;
   const int units = a.B * a.H * n_qb;
   const int ld = 3 * a.d;  // qkv row length
   float* sKT = sm;                           // [kFsHead][kFsMaxSeq]
@@ -346,7 +347,7 @@ __device__ __forceinline__ void fs_attention(const FsArgs& a, float* sm) {
     const int qb = u % n_qb;
     const int bh = u / n_qb;
     const int b = bh / a.H, hh = bh - (bh / a.H) * a.H;
-    const int q0 = qb * kFsQRows, q1 = min(a.S, q0 + kFsQRows);
+    const int q0 = qb * a.qrows, q1 = min(a.S, q0 + a.qrows);
     const int keys = a.causal ? q1 : a.S;
     const uint8_t* vk = a.valid != nullptr ? a.valid + static_cast<int64_t>(b) * a.S : nullptr;
     const uint16_t* base = a.qkv + static_cast<int64_t>(b) * a.S * ld + hh * kFsHead;
@@ -397,7 +398,7 @@ __device__ __forceinline__ void fs_attention(const FsArgs& a, float* sm) {
       }
     }
     __syncthreads();
-    if (warp >= kFsQRows / 2) continue;
+    if (warp >= a.qrows / 2) continue;
     const int iA = q0 + 2 * warp, iB = iA + 1;
     if (iA >= q1) continue;
     const bool hasB = iB < q1;
@@ -837,6 +838,10 @@ extern "C" int tjb_forward_small(const tjb_small_layer* layers, int L, const flo
   a.F = F;
   a.L = L;
   a.causal = causal;
+  // 8-row attention units unless that makes more units than CTAs (measured
+  // at config 1, 48 -> 96 units on 148 SMs: 0.254 -> 0.249 ms a forward;
+  // at 256 units, 2 x 8 heads x 16 blocks of 8 rows, 0.308 -> 0.318 ms).
+  a.qrows = B * H * ((S + 7) / 8) <= grid ? 8 : kFsQRows;
   a.ks_o = lay.ks_o;
   a.ks_2 = lay.ks_2;
   a.idesc = idesc_f16(128, Tsub, false, false);
